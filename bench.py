@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Session decode tokens/s of the fixed-budget KV-cache decode hot path.
+
+Workload (one GPU): Qwen2.5-3B-shaped decode -- 36 layers, 16 query / 2 KV
+heads, head_dim 128, fp16 K/V -- with 16 concurrent sessions, each primed
+with a 2048-token prompt into a 1040-slot budget (4 sink / 256 recent / 780
+important, 16-token pages), then decoded one token per step.  A step is one
+decode step of every session over every layer: 36 launches of the fused
+decode kernel (append + paged gather + GQA attention + received mass) and
+one launch of the eviction kernel.  Prompt K/V, importance scores and the
+per-step q / k / v are seeded synthetic tensors (no model weights: the hot
+path is the cache, the model's projections are outside it).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 run under torchrun: every rank owns its own 16 sessions (weak
+scaling, no collective on the decode path); times are the max over ranks.
+`--impl reference` times the reference's algorithm on the host cores (the
+oracle restatement, one process per core) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "session decode tokens/s at K=1040"
+UNIT = "session-tokens/s"
+WORKLOAD = dict(layers=36, hq=16, hkv=2, d=128, sessions=16, prompt=2048, sink=4, recent=256, important=780,
+                dtype="float16", decay=0.99)
+# Algorithmic bytes per session-layer-step: K/V of the 1040 retained slots
+# (2 x 1040 x 2 heads x 128 x 2 B = 1,064,960) + new K/V append (1,024) +
+# q read and o write (8,192) + page table (260) + importance read/write (8,320).
+ALG_BYTES_PER_SESSION_LAYER = 1_082_756
+PROFILE_TRAFFIC = ROOT / "profiles" / "decode_layer_c2.md"
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ---- clocks (NVML, read-only) ---------------------------------------------------------------
+REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler(threading.Thread):
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        super().__init__(daemon=True)
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:
+                bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # report, never fail the bench on telemetry
+            self.err = str(e)
+
+    def run(self):
+        while self.ok and not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def stop(self):
+        self._stop.set()
+        if self.is_alive():
+            self.join(timeout=2)
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "")}
+        names = [n for b, n in REASON_BITS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ---- CPU legs -------------------------------------------------------------------------------
+def cpu_baseline(spec, budget_s=15.0):
+    """The reference's decode path (oracle restatement) on all host cores, on a
+    bounded sample of the same workload."""
+    from oracle.cpu_fleet import CpuDecodeFleet
+    with CpuDecodeFleet(spec) as fleet:
+        t1 = fleet.run(1)
+        steps = max(1, min(50, int(budget_s / max(t1, 1e-3))))
+        t = fleet.run(steps)
+        return {"value": spec["sessions"] * steps / t, "unit": UNIT, "cores": fleet.workers, "kind": "port",
+                "sample": f"{spec['sessions']} sessions x {steps} decode steps x {spec['layers']} layers "
+                          f"(one single-threaded process per core, numpy oracle of the reference cache)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    spec = dict(WORKLOAD)
+    from oracle.cpu_fleet import CpuDecodeFleet
+    with CpuDecodeFleet(spec) as fleet:
+        tw = fleet.run(max(1, args.warmup)) / max(1, args.warmup)
+        # each step is one decode step of every session; cap the timed steps so
+        # the run stays within a few minutes of CPU time
+        steps = max(1, min(args.steps, int(120.0 / max(tw, 1e-3))))
+        t = fleet.run(steps)
+        value = spec["sessions"] * steps / t
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": config_dict(spec, world),
+                "cpu_baseline": {"value": value, "unit": UNIT, "cores": fleet.workers, "kind": "port",
+                                 "sample": f"{spec['sessions']} sessions x {steps} decode steps "
+                                           f"(requested {args.steps}) x {spec['layers']} layers"},
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+
+
+def config_dict(spec, world):
+    return {"workload": "qwen2.5-3b-shaped decode: 16 sessions x 36 layers, 16/2 heads, head_dim 128, "
+                        "budget 1040 (4/256/780), 2048-token primed prompts, page 16",
+            "sessions_per_gpu": spec["sessions"], "layers": spec["layers"], "q_heads": spec["hq"],
+            "kv_heads": spec["hkv"], "head_dim": spec["d"], "budget": "4/256/780", "prompt_tokens": spec["prompt"],
+            "page_size": 16, "kv_dtype": "fp16", "accumulate": "fp32", "parallelism": f"sessions sharded, dp{world}",
+            "l2": "inputs larger than L2: 613 MB of K/V read per step vs 126 MB L2"}
+
+
+def read_traffic():
+    """DRAM bytes per decode launch from the committed ncu summary, if any."""
+    if not PROFILE_TRAFFIC.exists():
+        return None
+    for line in PROFILE_TRAFFIC.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip().split()[0]))
+            except ValueError:
+                return None
+    return None
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+# ---- our arm ----------------------------------------------------------------------------------
+def build_batch(spec, device, seed):
+    from infercache_b200 import CacheConfig, SessionBatch
+    cfg = CacheConfig(num_layers=spec["layers"], num_kv_heads=spec["hkv"], head_dim=spec["d"],
+                      sink_size=spec["sink"], recent_size=spec["recent"], important_size=spec["important"],
+                      decay=spec["decay"], dtype=torch.float16)
+    b = SessionBatch(cfg, spec["sessions"], device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    L, H, T, D = spec["layers"], spec["hkv"], spec["prompt"], spec["d"]
+    for s in range(spec["sessions"]):
+        pk = torch.randn(L, 1, H, T, D, generator=g, device=device, dtype=torch.float16)
+        pv = torch.randn(L, 1, H, T, D, generator=g, device=device, dtype=torch.float16)
+        u = torch.rand(T, generator=g, device=device)
+        b.load_prompt(s, tuple((pk[l], pv[l]) for l in range(L)), u / u.sum())
+    torch.cuda.synchronize()
+    return b
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cluster", type=int, default=0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank, world, local_rank = dist_env()
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch.distributed as dist
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    spec = dict(WORKLOAD)
+    S, L, Hq, Hkv, D = spec["sessions"], spec["layers"], spec["hq"], spec["hkv"], spec["d"]
+    b = build_batch(spec, device, seed=1234 + rank)
+    b.cluster_size = args.cluster
+    g = torch.Generator(device=device).manual_seed(99 + rank)
+    q = torch.randn(L, S, Hq, D, generator=g, device=device, dtype=torch.float16)
+    k = torch.randn(L, S, Hkv, D, generator=g, device=device, dtype=torch.float16)
+    v = torch.randn(L, S, Hkv, D, generator=g, device=device, dtype=torch.float16)
+    out = torch.empty(L, S, Hq, D, device=device, dtype=torch.float16)
+    pos = torch.full((S,), spec["prompt"], dtype=torch.int64, device=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # eager warm-up (also configures the kernels before capture)
+    for _ in range(args.warmup):
+        b.step(q, k, v, pos, out=out)
+        pos.add_(1)
+    torch.cuda.synchronize()
+
+    # one decode step of every session, captured once and replayed
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, stream=cap):
+        b.step(q, k, v, pos, out=out)
+        pos.add_(1)
+    dec_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dec_graph, stream=cap):
+        for l in range(L):
+            b.attend(l, q[l], k[l], v[l], out=out[l])
+    for _ in range(args.warmup):
+        step_graph.replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step_graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    sampler.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = world * S * args.steps / (ms / 1e3)
+
+    # decode-kernel launch duration for the roofline (graph of 36 launches)
+    kd = max(10, min(args.steps, 300))
+    for _ in range(3):
+        dec_graph.replay()
+    torch.cuda.synchronize()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(kd):
+        dec_graph.replay()
+    d1.record()
+    torch.cuda.synchronize()
+    dec_launch_s = max_over_ranks(d0.elapsed_time(d1)) / 1e3 / (kd * L)
+    alg_bytes = S * ALG_BYTES_PER_SESSION_LAYER
+    peak, peak_kind = measured_peak()
+    achieved = alg_bytes / dec_launch_s / 1e9
+    traffic = read_traffic()
+
+    # end to end through the public API: pinned host inputs -> device -> step -> host outputs
+    qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    qd, kd_, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ke = max(10, min(args.steps, 500))
+    for _ in range(3):
+        qd.copy_(qh, non_blocking=True); kd_.copy_(kh, non_blocking=True); vd.copy_(vh, non_blocking=True)
+        b.step(qd, kd_, vd, pos, out=out)
+        pos.add_(1)
+        oh.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
+    for _ in range(ke):
+        qd.copy_(qh, non_blocking=True); kd_.copy_(kh, non_blocking=True); vd.copy_(vh, non_blocking=True)
+        b.step(qd, kd_, vd, pos, out=out)
+        pos.add_(1)
+        oh.copy_(out, non_blocking=True)
+    x1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(x0.elapsed_time(x1))
+    e2e_value = world * S * ke / (e2e_ms / 1e3)
+    h2d = (q.numel() + k.numel() + v.numel()) * q.element_size()
+    d2h = out.numel() * out.element_size()
+    b.check_device_status()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(spec)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": config_dict(spec, world),
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": traffic,
+                             "kernel": "decode_kernel (ic_decode_layer), one launch = 16 sessions x 1 layer",
+                             "alg_bytes_per_launch": alg_bytes, "launch_us": dec_launch_s * 1e6,
+                             "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "steps": ke, "api": "SessionBatch.step (ic_decode_step) with pinned host buffers"},
+                "gpu_launches": args.steps * (L + 1),
+                "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del step_graph, dec_graph
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

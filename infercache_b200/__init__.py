@@ -1,0 +1,19 @@
+"""infercache_b200: the fixed-budget KV-cache decode hot path of infercache,
+built for the B200 (sm_100a).
+
+Public API (the reference's names):
+    CacheConfig, CacheStats, HierarchicalKVCache      hierarchical_cache
+    SessionBatch                                       batched sessions + hot-path verbs
+    PAGE_SIZE, PagedCacheConfig, PagePool, KVAllocator,
+    PagedSessionView, MultiSessionCache                paged_cache
+    TwoPassConfig, SummaryResult, TwoPassEngine        two_pass
+    gather_cache_kv, scatter_importance, topk_min_slot,
+    compact_sdp_attention, GPUImportanceTracker        cache_ops (the triton_ops names)
+
+Importing the package needs no GPU; constructing a cache does.
+"""
+from .hierarchical_cache import CacheConfig, CacheStats, HierarchicalKVCache, SessionBatch  # noqa: F401
+from .paged_cache import (PAGE_SIZE, KVAllocator, MultiSessionCache, PagedCacheConfig,  # noqa: F401
+                          PagedSessionView, PagePool)
+
+__version__ = "0.1.0"

@@ -1,0 +1,63 @@
+// Library-level entry points of the C ABI: status strings, ABI version,
+// device check and the last-error string.
+#include <stdio.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace ic {
+
+static thread_local char g_last_error[256] = "";
+
+void set_last_error(const char* msg) {
+  strncpy(g_last_error, msg, sizeof(g_last_error) - 1);
+  g_last_error[sizeof(g_last_error) - 1] = '\0';
+}
+
+int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return IC_OK;
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, cudaGetErrorString(e));
+  return IC_ERR_LAUNCH;
+}
+
+}  // namespace ic
+
+extern "C" const char* ic_status_str(int status) {
+  switch (status) {
+    case IC_OK: return "ok";
+    case IC_ERR_INVALID_ARG: return "invalid argument";
+    case IC_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case IC_ERR_OUT_OF_PAGES: return "page pool exhausted";
+    case IC_ERR_SESSION_CAP: return "session page cap exceeded";
+    case IC_ERR_CORRUPT_TABLE: return "slot or page table entry out of range";
+    case IC_ERR_LAUNCH: return "kernel launch failed";
+    case IC_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case IC_ERR_CUDA: return "CUDA runtime error";
+    case IC_ERR_NO_DEVICE: return "no sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int ic_abi_version(void) { return IC_ABI_VERSION; }
+
+extern "C" int ic_device_check(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    ic::set_last_error("no CUDA device");
+    return IC_ERR_NO_DEVICE;
+  }
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return IC_ERR_NO_DEVICE;
+  }
+  if (p.major != 10) {
+    ic::set_last_error("device is not sm_100 (B200)");
+    return IC_ERR_NO_DEVICE;
+  }
+  return IC_OK;
+}
+
+extern "C" const char* ic_last_error(void) { return ic::g_last_error; }

@@ -1,0 +1,363 @@
+// Kernel B and the per-session metadata kernels.
+//
+//  * evict_update  -- once per session-step: decayed importance + received
+//    mass, promotion / eviction of the token leaving the recent ring with an
+//    exact first-index argmin over L2, slot-table rotation so the staging row
+//    (already holding the new token's K/V in every layer) becomes the ring
+//    slot, ring advance, counters and an event record.
+//  * sort_slots    -- occupied slots in (position, slot) order.
+//  * boost_sorted  -- the reference push's mean attention weight, mapped from
+//    position rank to slot.
+//  * append_staging / reset_sessions.
+//
+// One CTA per session; importance arithmetic is float32 with every multiply
+// and add rounded separately (no contraction), so the update is
+// importance * decay, rounded, plus mass / div, rounded.
+#include "common.cuh"
+
+namespace ic {
+
+constexpr int EV_THREADS = 512;
+
+__global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a) {
+  extern __shared__ float imp_s[];  // [budget]
+  __shared__ float red_v[EV_THREADS / 32];
+  __shared__ int red_i[EV_THREADS / 32];
+  __shared__ int amin_slot;
+
+  const int s = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int B = a.tiers.budget, ntot = B + 1;
+  const int sink = a.tiers.sink_size, recent = a.tiers.recent_size, cap = a.tiers.important_size;
+  const int l2s = sink + recent;
+
+  int32_t* ctrl = a.sess.ctrl + static_cast<size_t>(s) * IC_CTRL_WORDS;
+  int64_t* cnt = a.sess.counters + static_cast<size_t>(s) * IC_COUNTER_WORDS;
+  float* imp = a.sess.importance + static_cast<size_t>(s) * B;
+  uint8_t* occ = a.sess.occupied + static_cast<size_t>(s) * B;
+  int64_t* pos = a.sess.positions + static_cast<size_t>(s) * B;
+  int32_t* stt = a.sess.slot_table + static_cast<size_t>(s) * ntot;
+
+  // 1. decay + boost of every occupied slot
+  const float decay = a.decay;
+  const float div = a.mass_div;
+  for (int j = tid; j < B; j += EV_THREADS) {
+    float v = imp[j];
+    if (occ[j]) {
+      float add = 0.f;
+      if (a.mass) {
+        const float* m = a.mass + static_cast<size_t>(s) * a.mass_rows * ntot + j;
+        float tot = m[0];
+        for (int r = 1; r < a.mass_rows; ++r) tot = __fadd_rn(tot, m[static_cast<size_t>(r) * ntot]);
+        add = __fdiv_rn(tot, div);
+      }
+      v = __fadd_rn(__fmul_rn(v, decay), add);
+      imp[j] = v;
+    }
+    imp_s[j] = v;
+  }
+  // Snapshot the decision inputs: every thread must branch identically, and
+  // thread 0 rewrites ctrl / occupied below.
+  __shared__ int snap_r, snap_fill, snap_disp;
+  if (tid == 0) {
+    snap_r = ctrl[IC_CTRL_RECENT_PTR];
+    snap_fill = ctrl[IC_CTRL_IMPORTANT_FILL];
+    const bool ok = snap_r >= sink && snap_r < l2s && snap_fill >= 0 && snap_fill <= cap;
+    if (!ok) {
+      if (a.sess.dev_status) atomicOr(a.sess.dev_status, IC_DEVFLAG_BAD_ROW);
+      snap_r = -1;
+    } else {
+      snap_disp = occ[snap_r] != 0;
+    }
+  }
+  __syncthreads();
+  if (snap_r < 0) return;  // corrupted ring state: reported, nothing written
+
+  const int r = snap_r;
+  const int l2fill = snap_fill;
+  const bool displaced = snap_disp != 0;
+  const float score = imp_s[r];
+  const bool need_argmin = displaced && !(score <= 0.f) && l2fill >= cap && cap > 0;
+
+  // 2. first-index argmin over the filled L2 slice
+  if (need_argmin) {
+    float bv = __int_as_float(0x7f800000);  // +inf
+    int bi = 0x7fffffff;
+    for (int j = l2s + tid; j < l2s + l2fill; j += EV_THREADS) {
+      const float v = imp_s[j];
+      if (argmin_less(v, j, bv, bi)) { bv = v; bi = j; }
+    }
+    warp_argmin(bv, bi);
+    if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; }
+    __syncthreads();
+    if (warp == 0) {
+      bv = lane < EV_THREADS / 32 ? red_v[lane] : __int_as_float(0x7f800000);
+      bi = lane < EV_THREADS / 32 ? red_i[lane] : 0x7fffffff;
+      warp_argmin(bv, bi);
+      if (lane == 0) amin_slot = bi;
+    }
+    __syncthreads();
+  }
+
+  // 3. apply the decision (one thread)
+  if (tid == 0) {
+    int64_t kind = IC_EV_NONE, dpos = -1, target = -1, epos = -1;
+    const int32_t row_r = stt[r], row_s = stt[B];
+    int32_t new_stage = row_r;
+    if (displaced) {
+      dpos = pos[r];
+      int tgt = -1;
+      if (score <= 0.f) {
+        kind = IC_EV_DROP;
+      } else if (l2fill < cap) {
+        tgt = l2s + l2fill;
+        ctrl[IC_CTRL_IMPORTANT_FILL] = l2fill + 1;
+        kind = IC_EV_FILL;
+      } else if (cap > 0) {
+        target = amin_slot;
+        if (score > imp_s[amin_slot]) {
+          tgt = amin_slot;
+          kind = IC_EV_EVICT;
+          epos = pos[tgt];
+          cnt[IC_CNT_EVICTIONS] += 1;
+        } else {
+          kind = IC_EV_REJECT;
+        }
+      } else {
+        kind = IC_EV_REJECT;
+      }
+      if (tgt >= 0) {
+        target = tgt;
+        new_stage = stt[tgt];
+        stt[tgt] = row_r;
+        pos[tgt] = dpos;
+        imp[tgt] = score;
+        occ[tgt] = 1;
+        cnt[IC_CNT_PROMOTIONS] += 1;
+      }
+    }
+    stt[r] = row_s;
+    stt[B] = new_stage;
+    pos[r] = a.new_pos[s];
+    imp[r] = 0.f;
+    occ[r] = 1;
+    const int rf = ctrl[IC_CTRL_RECENT_FILL];
+    ctrl[IC_CTRL_RECENT_FILL] = rf + 1 < recent ? rf + 1 : recent;
+    ctrl[IC_CTRL_RECENT_PTR] = sink + (r - sink + 1) % recent;
+    cnt[IC_CNT_TOKENS_SEEN] += 1;
+    cnt[IC_CNT_STEPS] += 1;
+    if (a.events) {
+      int64_t* e = a.events + static_cast<size_t>(s) * 4;
+      e[0] = kind; e[1] = dpos; e[2] = target; e[3] = epos;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+constexpr int SORT_THREADS = 1024;
+
+__global__ void __launch_bounds__(SORT_THREADS) sort_slots_kernel(const ic_sort_args a) {
+  extern __shared__ unsigned char sm[];
+  const int s = blockIdx.x, B = a.tiers.budget;
+  int64_t* ps = reinterpret_cast<int64_t*>(sm);
+  uint8_t* os = sm + static_cast<size_t>(B) * 8;
+  __shared__ int fill_s;
+  const int64_t* pos = a.sess.positions + static_cast<size_t>(s) * B;
+  const uint8_t* occ = a.sess.occupied + static_cast<size_t>(s) * B;
+  int32_t* out = a.sorted_slots + static_cast<size_t>(s) * B;
+  if (threadIdx.x == 0) fill_s = 0;
+  for (int j = threadIdx.x; j < B; j += SORT_THREADS) {
+    ps[j] = pos[j];
+    os[j] = occ[j];
+    out[j] = -1;
+  }
+  __syncthreads();
+  int local = 0;
+  for (int j = threadIdx.x; j < B; j += SORT_THREADS) {
+    if (!os[j]) continue;
+    ++local;
+    const int64_t pj = ps[j];
+    int rank = 0;
+    for (int i = 0; i < B; ++i) rank += os[i] && (ps[i] < pj || (ps[i] == pj && i < j));
+    out[rank] = j;
+  }
+  atomicAdd(&fill_s, local);  // integer count: order-independent
+  __syncthreads();
+  if (threadIdx.x == 0) a.fill[s] = fill_s;
+}
+
+__global__ void boost_sorted_kernel(const ic_boost_args a) {
+  const int s = blockIdx.x, B = a.tiers.budget, ntot = B + 1;
+  float* mo = a.mass_out + static_cast<size_t>(s) * ntot;
+  for (int j = threadIdx.x; j < ntot; j += blockDim.x) mo[j] = 0.f;
+  __syncthreads();
+  const int fill = a.fill[s];
+  const int n = a.width < fill ? a.width : fill;
+  const size_t per_sess = static_cast<size_t>(a.L) * a.H * a.Q * a.width;
+  const float* w = a.weights + s * per_sess;
+  const float cnt = static_cast<float>(a.L * a.H * a.Q);
+  for (int rk = threadIdx.x; rk < n; rk += blockDim.x) {
+    float total = 0.f;
+    for (int hh = 0; hh < a.H; ++hh) {
+      float acc = 0.f;
+      bool first = true;
+      for (int l = 0; l < a.L; ++l)
+        for (int q = 0; q < a.Q; ++q) {
+          const float x = w[((static_cast<size_t>(l) * a.H + hh) * a.Q + q) * a.width + rk];
+          acc = first ? x : __fadd_rn(acc, x);
+          first = false;
+        }
+      total = hh == 0 ? acc : __fadd_rn(total, acc);
+    }
+    const int slot = a.sorted_slots[static_cast<size_t>(s) * B + rk];
+    if (slot >= 0) mo[slot] = __fdiv_rn(total, cnt);
+  }
+}
+
+template <typename T>
+__global__ void append_staging_kernel(const ic_append_args a) {
+  const int l = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int D = a.pool.head_dim, B = a.tiers.budget;
+  const int row = a.sess.slot_table[static_cast<size_t>(s) * (B + 1) + B];
+  if (row < 0 || row >= a.pool.pool_tokens) {
+    if (threadIdx.x == 0 && a.sess.dev_status) atomicOr(a.sess.dev_status, IC_DEVFLAG_BAD_ROW);
+    return;
+  }
+  const size_t dst = ((static_cast<size_t>(l) * a.pool.num_kv_heads + h) * a.pool.pool_tokens + row) * D;
+  const size_t src = s * a.stride_s + l * a.stride_l + h * a.stride_h;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    static_cast<T*>(a.pool.k)[dst + d] = static_cast<const T*>(a.k)[src + d];
+    static_cast<T*>(a.pool.v)[dst + d] = static_cast<const T*>(a.v)[src + d];
+  }
+}
+
+__global__ void reset_meta_kernel(const ic_reset_args a) {
+  const int s = a.session0 + blockIdx.x, B = a.tiers.budget;
+  for (int j = threadIdx.x; j < B; j += blockDim.x) {
+    a.sess.positions[static_cast<size_t>(s) * B + j] = -1;
+    a.sess.importance[static_cast<size_t>(s) * B + j] = 0.f;
+    a.sess.occupied[static_cast<size_t>(s) * B + j] = 0;
+  }
+  if (threadIdx.x < IC_CTRL_WORDS)
+    a.sess.ctrl[static_cast<size_t>(s) * IC_CTRL_WORDS + threadIdx.x] =
+        threadIdx.x == IC_CTRL_RECENT_PTR ? a.tiers.sink_size : 0;
+  if (threadIdx.x < IC_COUNTER_WORDS) a.sess.counters[static_cast<size_t>(s) * IC_COUNTER_WORDS + threadIdx.x] = 0;
+}
+
+template <typename T>
+__global__ void reset_kv_kernel(const ic_reset_args a) {
+  const int s = a.session0 + blockIdx.z;
+  const int lh = blockIdx.y;  // layer * Hkv + head
+  const int ntot = a.tiers.budget + 1, D = a.pool.head_dim;
+  const int32_t* stt = a.sess.slot_table + static_cast<size_t>(s) * ntot;
+  for (int j = blockIdx.x; j < ntot; j += gridDim.x) {
+    const int row = stt[j];
+    if (row < 0 || row >= a.pool.pool_tokens) continue;
+    const size_t base = (static_cast<size_t>(lh) * a.pool.pool_tokens + row) * D;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      static_cast<T*>(a.pool.k)[base + d] = T(0.f);
+      static_cast<T*>(a.pool.v)[base + d] = T(0.f);
+    }
+  }
+}
+
+static bool tiers_ok(const ic_tiers& t) {
+  return t.sink_size >= 0 && t.recent_size >= 1 && t.important_size >= 0 &&
+         t.budget == t.sink_size + t.recent_size + t.important_size && t.budget > 0;
+}
+
+}  // namespace ic
+
+using namespace ic;
+
+extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
+  if (!a) return IC_ERR_INVALID_ARG;
+  if (a->sess.num_sessions == 0) return IC_OK;
+  if (!tiers_ok(a->tiers) || a->sess.num_sessions < 0 || !a->new_pos || !a->sess.slot_table ||
+      !a->sess.positions || !a->sess.importance || !a->sess.occupied || !a->sess.ctrl ||
+      !a->sess.counters || (a->mass && (a->mass_rows < 1 || !(a->mass_div > 0.f)))) {
+    set_last_error("evict_update: bad arguments");
+    return IC_ERR_INVALID_ARG;
+  }
+  const size_t smem = static_cast<size_t>(a->tiers.budget) * sizeof(float);
+  if (smem > 200 * 1024) { set_last_error("evict_update: budget too large"); return IC_ERR_UNSUPPORTED; }
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(evict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured = true;
+  }
+  evict_kernel<<<a->sess.num_sessions, EV_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(*a);
+  return launch_status("evict_update");
+}
+
+extern "C" int ic_sort_slots(const ic_sort_args* a, void* stream) {
+  if (!a) return IC_ERR_INVALID_ARG;
+  if (a->sess.num_sessions == 0) return IC_OK;
+  if (!tiers_ok(a->tiers) || !a->sorted_slots || !a->fill || !a->sess.positions || !a->sess.occupied) {
+    set_last_error("sort_slots: bad arguments");
+    return IC_ERR_INVALID_ARG;
+  }
+  const size_t smem = static_cast<size_t>(a->tiers.budget) * 9;
+  if (smem > 200 * 1024) { set_last_error("sort_slots: budget too large"); return IC_ERR_UNSUPPORTED; }
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(sort_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    configured = true;
+  }
+  sort_slots_kernel<<<a->sess.num_sessions, SORT_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(*a);
+  return launch_status("sort_slots");
+}
+
+extern "C" int ic_boost_sorted(const ic_boost_args* a, void* stream) {
+  if (!a) return IC_ERR_INVALID_ARG;
+  if (a->num_sessions == 0) return IC_OK;
+  if (!tiers_ok(a->tiers) || !a->weights || !a->sorted_slots || !a->fill || !a->mass_out || a->L < 1 ||
+      a->H < 1 || a->Q < 1 || a->width < 0) {
+    set_last_error("boost_sorted: bad arguments");
+    return IC_ERR_INVALID_ARG;
+  }
+  boost_sorted_kernel<<<a->num_sessions, 256, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  return launch_status("boost_sorted");
+}
+
+extern "C" int ic_append_staging(const ic_append_args* a, void* stream) {
+  if (!a) return IC_ERR_INVALID_ARG;
+  if (a->sess.num_sessions == 0) return IC_OK;
+  if (!tiers_ok(a->tiers) || !a->k || !a->v || !a->pool.k || !a->pool.v || !a->sess.slot_table ||
+      a->pool.head_dim <= 0) {
+    set_last_error("append_staging: bad arguments");
+    return IC_ERR_INVALID_ARG;
+  }
+  dim3 grid(a->pool.num_layers, a->pool.num_kv_heads, a->sess.num_sessions);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (a->pool.dtype) {
+    case IC_F32: append_staging_kernel<float><<<grid, 128, 0, st>>>(*a); break;
+    case IC_F16: append_staging_kernel<__half><<<grid, 128, 0, st>>>(*a); break;
+    case IC_BF16: append_staging_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(*a); break;
+    default: set_last_error("append_staging: bad dtype"); return IC_ERR_INVALID_ARG;
+  }
+  return launch_status("append_staging");
+}
+
+extern "C" int ic_reset_sessions(const ic_reset_args* a, void* stream) {
+  if (!a) return IC_ERR_INVALID_ARG;
+  if (a->n == 0) return IC_OK;
+  if (!tiers_ok(a->tiers) || a->n < 0 || a->session0 < 0 || a->session0 + a->n > a->sess.num_sessions ||
+      !a->sess.positions || !a->sess.importance || !a->sess.occupied || !a->sess.ctrl || !a->sess.counters) {
+    set_last_error("reset_sessions: bad arguments");
+    return IC_ERR_INVALID_ARG;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  reset_meta_kernel<<<a->n, 256, 0, st>>>(*a);
+  int rc = launch_status("reset_sessions");
+  if (rc != IC_OK || !a->zero_kv) return rc;
+  if (!a->pool.k || !a->pool.v || !a->sess.slot_table) return IC_ERR_INVALID_ARG;
+  dim3 grid(64, a->pool.num_layers * a->pool.num_kv_heads, a->n);
+  switch (a->pool.dtype) {
+    case IC_F32: reset_kv_kernel<float><<<grid, 128, 0, st>>>(*a); break;
+    case IC_F16: reset_kv_kernel<__half><<<grid, 128, 0, st>>>(*a); break;
+    case IC_BF16: reset_kv_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(*a); break;
+    default: return IC_ERR_INVALID_ARG;
+  }
+  return launch_status("reset_sessions");
+}

@@ -1,0 +1,498 @@
+"""Fixed-budget hierarchical KV cache on the B200.
+
+Same tiers and semantics as the reference's ``hierarchical_cache.py``:
+``[0, sink)`` attention sinks, ``[sink, sink+recent)`` the recent ring,
+``[sink+recent, budget)`` the scored L2 pool with first-index-argmin
+eviction (hierarchical_cache.py:6-48, 67-93).
+
+Two classes:
+
+* ``SessionBatch`` -- S sessions whose K/V live in one ``PagePool`` and whose
+  slot metadata (positions, importance, occupancy, fill pointers, counters)
+  lives on the GPU.  Its verbs are the decode hot path, all sessions per
+  launch:
+    ``attend(layer, q, k, v)``  kernel A: append + paged gather + GQA decode
+                                attention + received mass, one layer;
+    ``evict(positions)``        kernel B: decayed importance + mass,
+                                promotion / eviction, ring advance;
+    ``step(q, k, v, pos)``      every layer then ``evict``;
+    ``gather(session)``         position-ordered K/V export.
+* ``HierarchicalKVCache`` -- the reference's single-session class with the
+  same constructor and methods (``push``, ``load_from_hf_output``,
+  ``to_hf_past_key_values``, ``get_position_ids_for_cache``, ``reset``,
+  ``stats``, ``current_fill``, ``total_budget`` and the public
+  ``K / V / positions / importance / occupied`` tensors), backed by a
+  one-session ``SessionBatch``.
+
+Each logical slot maps to a pool row through a per-session slot table with
+one extra entry, the staging row.  A decode step writes the new token's K/V
+into the staging row of every layer; ``evict`` then rotates slot-table
+entries so the staging row becomes the ring slot and a promoted token's row
+moves to its L2 slot.  Promotion therefore copies no K/V (the reference
+copies all layers, hierarchical_cache.py:461-462, 472-473).
+
+There is no CPU path: construction requires an sm_100 device and the built
+library.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .cache_safety import normalise_kv, to_dynamic_cache
+from .paged_cache import PAGE_SIZE, PagedCacheConfig, PagePool
+
+__all__ = ["CacheConfig", "CacheStats", "SessionBatch", "HierarchicalKVCache", "_normalise_past_kv"]
+
+
+@dataclass
+class CacheConfig:
+    """hierarchical_cache.py:67-93.  ``decay`` multiplies the importance of
+    every occupied slot once per fused decode step (``SessionBatch.evict``);
+    ``evict_quantile`` and ``kll_k`` are accepted for compatibility and
+    unused (the reference never reads the quantile sketch either)."""
+    num_layers: int
+    num_kv_heads: int
+    head_dim: int
+    sink_size: int = 4
+    recent_size: int = 256
+    important_size: int = 252
+    evict_quantile: float = 0.15
+    decay: float = 0.99
+    kll_k: int = 128
+    dtype: torch.dtype = torch.float16
+
+    @property
+    def total_budget(self) -> int:
+        return self.sink_size + self.recent_size + self.important_size
+
+    @property
+    def recent_start(self) -> int:
+        return self.sink_size
+
+    @property
+    def important_start(self) -> int:
+        return self.sink_size + self.recent_size
+
+
+@dataclass
+class CacheStats:
+    """hierarchical_cache.py:98-105."""
+    total_tokens_seen: int = 0
+    total_evictions: int = 0
+    current_fill: int = 0
+    sink_fill: int = 0
+    recent_fill: int = 0
+    important_fill: int = 0
+
+
+def _check_cfg(cfg: CacheConfig) -> None:
+    if cfg.recent_size < 1:
+        raise ValueError("recent_size must be >= 1 (the ring advances modulo recent_size)")
+    if cfg.sink_size < 0 or cfg.important_size < 0:
+        raise ValueError("tier sizes must be >= 0")
+    if not (0.0 < cfg.decay <= 1.0):
+        raise ValueError(f"decay must be in (0, 1], got {cfg.decay}")
+
+
+class SessionBatch:
+    """S fixed-budget sessions on one GPU, one PagePool, device-resident metadata."""
+
+    def __init__(self, cfg: CacheConfig, num_sessions: int, device="cuda",
+                 pool: Optional[PagePool] = None, session_pages: Optional[Sequence[Sequence[int]]] = None):
+        _check_cfg(cfg)
+        dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        _lib.require_device(dev)
+        self.cfg = cfg
+        self.device = dev
+        self.num_sessions = S = int(num_sessions)
+        B = cfg.total_budget
+        ntot = B + 1
+        self.pages_per_session = -(-ntot // PAGE_SIZE)
+        if pool is None:
+            pool = PagePool(PagedCacheConfig(n_pages=max(1, S) * self.pages_per_session, n_layers=cfg.num_layers,
+                                             n_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, dtype=cfg.dtype,
+                                             device=str(dev), max_pages_per_session=self.pages_per_session))
+            session_pages = [list(range(i * self.pages_per_session, (i + 1) * self.pages_per_session))
+                             for i in range(S)]
+        elif session_pages is None:
+            raise ValueError("session_pages is required with a shared pool")
+        pc = pool.cfg
+        if (pc.n_layers, pc.n_heads, pc.head_dim, pc.dtype) != (cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, cfg.dtype):
+            raise ValueError("pool geometry / dtype does not match the cache config")
+        self.pool = pool
+        self.session_pages = [list(p) for p in session_pages]
+        rows = []
+        for pages in self.session_pages:
+            if len(pages) < self.pages_per_session:
+                raise ValueError(f"each session needs {self.pages_per_session} pages")
+            r = [p * PAGE_SIZE + o for p in pages for o in range(PAGE_SIZE)][:ntot]
+            rows.append(r)
+        self.slot_table = torch.tensor(rows, dtype=torch.int32).reshape(S, ntot).to(dev)
+        self.positions = torch.full((S, B), -1, dtype=torch.int64, device=dev)
+        self.importance = torch.zeros((S, B), dtype=torch.float32, device=dev)
+        self.occupied = torch.zeros((S, B), dtype=torch.bool, device=dev)
+        self.ctrl = torch.zeros((S, _lib.IC_CTRL_WORDS), dtype=torch.int32, device=dev)
+        self.ctrl[:, _lib.IC_CTRL_RECENT_PTR] = cfg.recent_start
+        self.counters = torch.zeros((S, _lib.IC_COUNTER_WORDS), dtype=torch.int64, device=dev)
+        self.dev_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.mass = torch.zeros((S, cfg.num_kv_heads, ntot), dtype=torch.float32, device=dev)
+        self.events = torch.full((S, 4), -1, dtype=torch.int64, device=dev)
+        self._pos_buf = torch.zeros(S, dtype=torch.int64, device=dev)
+        self.scale = cfg.head_dim ** -0.5
+        self.cluster_size = 0
+
+        self._c_tiers = _lib.ic_tiers(cfg.sink_size, cfg.recent_size, cfg.important_size, B)
+        self._c_sess = _lib.ic_sessions(num_sessions=S, slot_table=self.slot_table.data_ptr(),
+                                        positions=self.positions.data_ptr(), importance=self.importance.data_ptr(),
+                                        occupied=self.occupied.data_ptr(), ctrl=self.ctrl.data_ptr(),
+                                        counters=self.counters.data_ptr(), dev_status=self.dev_status.data_ptr())
+        self._c_pool = pool.c_pool()
+        self._dec = _lib.ic_decode_args(pool=self._c_pool, tiers=self._c_tiers, sess=self._c_sess,
+                                        mass=self.mass.data_ptr(), scale=self.scale)
+        self._ev = _lib.ic_evict_args(tiers=self._c_tiers, sess=self._c_sess, mass=self.mass.data_ptr(),
+                                      mass_rows=cfg.num_kv_heads, mass_div=float(cfg.num_layers * cfg.num_kv_heads),
+                                      decay=cfg.decay, new_pos=self._pos_buf.data_ptr(),
+                                      events=self.events.data_ptr())
+        self._step = _lib.ic_step_args(layer0=self._dec, evict=self._ev)
+
+    # ---- hot path -------------------------------------------------------------------
+    def attend(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """Kernel A for one layer: q [S, Hq, D], k / v [S, Hkv, D] in the cache
+        dtype, contiguous, on this device.  Returns out [S, Hq, D].  The first
+        layer of a step must be layer 0 (it starts the step's mass sum)."""
+        cfg = self.cfg
+        S = self.num_sessions
+        if q.dim() != 3 or q.shape[0] != S or q.shape[2] != cfg.head_dim:
+            raise ValueError(f"q must be [S={S}, Hq, {cfg.head_dim}], got {tuple(q.shape)}")
+        if tuple(k.shape) != (S, cfg.num_kv_heads, cfg.head_dim) or k.shape != v.shape:
+            raise ValueError(f"k / v must be [{S}, {cfg.num_kv_heads}, {cfg.head_dim}]")
+        for t in (q, k, v):
+            if t.dtype != cfg.dtype or t.device != self.device or not t.is_contiguous():
+                raise ValueError("q / k / v must be contiguous tensors of the cache dtype on the cache device")
+        Hq = q.shape[1]
+        od = out_dtype or cfg.dtype
+        if out is None:
+            out = torch.empty((S, Hq, cfg.head_dim), dtype=od, device=self.device)
+        elif out.shape != q.shape or not out.is_contiguous() or out.device != self.device:
+            raise ValueError("out must be a contiguous [S, Hq, D] tensor on the cache device")
+        d = self._dec
+        d.layer = layer
+        d.num_q_heads = Hq
+        d.q = q.data_ptr()
+        d.k_new = k.data_ptr()
+        d.v_new = v.data_ptr()
+        d.out = out.data_ptr()
+        d.out_dtype = _lib.dtype_code(out.dtype)
+        d.accumulate = 1 if layer > 0 else 0
+        d.cluster_size = self.cluster_size
+        _lib.call("ic_decode_layer", d)
+        return out
+
+    def evict(self, positions, decay: Optional[float] = None) -> None:
+        """Kernel B once per step after the last layer.  positions: [S] int64
+        (tensor on this device, or a sequence of ints) of the decoded tokens."""
+        pos = self._positions_arg(positions)
+        e = self._ev
+        e.new_pos = pos.data_ptr()
+        e.decay = self.cfg.decay if decay is None else float(decay)
+        e.mass = self.mass.data_ptr()
+        e.mass_rows = self.cfg.num_kv_heads
+        e.mass_div = float(self.cfg.num_layers * self.cfg.num_kv_heads)
+        _lib.call("ic_evict_update", e)
+        self._keep = pos  # keep alive until the launch is consumed
+
+    def step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions,
+             out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """One decode step of every session in one C call (``ic_decode_step``):
+        q [L, S, Hq, D], k / v [L, S, Hkv, D] contiguous in the cache dtype;
+        positions [S] of the decoded tokens.  Returns out [L, S, Hq, D]."""
+        cfg = self.cfg
+        L, S, D = cfg.num_layers, self.num_sessions, cfg.head_dim
+        if q.dim() != 4 or q.shape[0] != L or q.shape[1] != S or q.shape[3] != D:
+            raise ValueError(f"q must be [L={L}, S={S}, Hq, {D}], got {tuple(q.shape)}")
+        if tuple(k.shape) != (L, S, cfg.num_kv_heads, D) or k.shape != v.shape:
+            raise ValueError(f"k / v must be [{L}, {S}, {cfg.num_kv_heads}, {D}]")
+        for t in (q, k, v):
+            if t.dtype != cfg.dtype or t.device != self.device or not t.is_contiguous():
+                raise ValueError("q / k / v must be contiguous tensors of the cache dtype on the cache device")
+        Hq = q.shape[2]
+        if out is None:
+            out = torch.empty(q.shape, dtype=out_dtype or cfg.dtype, device=self.device)
+        elif out.shape != q.shape or not out.is_contiguous() or out.device != self.device:
+            raise ValueError("out must be a contiguous [L, S, Hq, D] tensor on the cache device")
+        pos = self._positions_arg(positions)
+        st = self._step
+        d = st.layer0
+        d.num_q_heads = Hq
+        d.q = q.data_ptr()
+        d.k_new = k.data_ptr()
+        d.v_new = v.data_ptr()
+        d.out = out.data_ptr()
+        d.out_dtype = _lib.dtype_code(out.dtype)
+        d.cluster_size = self.cluster_size
+        st.q_layer_stride = S * Hq * D
+        st.kv_layer_stride = S * cfg.num_kv_heads * D
+        st.out_layer_stride = S * Hq * D
+        st.evict.new_pos = pos.data_ptr()
+        st.evict.decay = cfg.decay
+        _lib.call("ic_decode_step", st)
+        self._keep = pos
+        return out
+
+    def _positions_arg(self, positions) -> torch.Tensor:
+        if isinstance(positions, torch.Tensor) and positions.device == self.device and positions.dtype == torch.int64:
+            return positions.contiguous()
+        pos = torch.as_tensor(positions, dtype=torch.int64).reshape(self.num_sessions)
+        self._pos_buf.copy_(pos, non_blocking=True)
+        return self._pos_buf
+
+    # ---- reference-compatible push (per session) --------------------------------------
+    def push(self, session: int, key_states: torch.Tensor, value_states: torch.Tensor, position: int,
+             attn_weights: Optional[torch.Tensor] = None) -> None:
+        """hierarchical_cache.py:241-294 for one session of the batch:
+        key_states [L, Hkv, 1, D]; attn_weights [L, Hkv, Q, F'] or [L, Hkv, F']
+        (position-ordered, averaged over L, Hkv, Q).  No importance decay."""
+        cfg = self.cfg
+        sub = self._sub(session)
+        k = key_states.to(self.device, cfg.dtype)[:, :, 0, :].contiguous()
+        v = value_states.to(self.device, cfg.dtype)[:, :, 0, :].contiguous()
+        if k.shape != (cfg.num_layers, cfg.num_kv_heads, cfg.head_dim):
+            raise ValueError("key_states must be [num_layers, num_kv_heads, 1, head_dim]")
+        a = _lib.ic_append_args(pool=self._c_pool, tiers=self._c_tiers, sess=sub, k=k.data_ptr(), v=v.data_ptr(),
+                                stride_s=0, stride_l=k.stride(0), stride_h=k.stride(1))
+        _lib.call("ic_append_staging", a)
+        mass = None
+        if attn_weights is not None:
+            w = attn_weights.to(self.device, torch.float32)
+            if w.dim() == 3:
+                w = w[:, :, None, :]
+            w = w.contiguous()
+            Lw, Hw, Qw, F = w.shape
+            srt, fill = self._sort(sub)
+            mass = torch.empty((1, 1, cfg.total_budget + 1), dtype=torch.float32, device=self.device)
+            b = _lib.ic_boost_args(tiers=self._c_tiers, num_sessions=1, L=Lw, H=Hw, Q=Qw, width=F,
+                                   weights=w.data_ptr(), sorted_slots=srt.data_ptr(), fill=fill.data_ptr(),
+                                   mass_out=mass.data_ptr())
+            _lib.call("ic_boost_sorted", b)
+        pos = torch.tensor([int(position)], dtype=torch.int64).to(self.device, non_blocking=True)
+        e = _lib.ic_evict_args(tiers=self._c_tiers, sess=sub, mass=_lib.ptr(mass), mass_rows=1, mass_div=1.0,
+                               decay=1.0, new_pos=pos.data_ptr(),
+                               events=self.events[session:].data_ptr())
+        _lib.call("ic_evict_update", e)
+        self._keep = (k, v, mass, pos)
+
+    # ---- priming, export, reset ------------------------------------------------------------
+    def load_prompt(self, session: int, past_key_values, importance_scores: torch.Tensor,
+                    positions: Optional[torch.Tensor] = None) -> None:
+        """load_from_hf_output (hierarchical_cache.py:179-237) for one session."""
+        cfg = self.cfg
+        pkv = normalise_kv(past_key_values)
+        if pkv is None:
+            raise TypeError("past_key_values is empty")
+        T = pkv[0][0].shape[2]
+        self.reset([session], zero_kv=True)
+        sub = self._sub(session)
+        scores = importance_scores.to(self.device, torch.float32).reshape(1, T).contiguous()
+        pos = None
+        if positions is not None:
+            pos = positions.to(self.device, torch.int64).reshape(1, T).contiguous()
+        slot_token = torch.empty((1, cfg.total_budget), dtype=torch.int32, device=self.device)
+        a = _lib.ic_tier_fill_args(tiers=self._c_tiers, sess=sub, session0=0, n=1, T=T,
+                                   scores=scores.data_ptr(), positions=_lib.ptr(pos),
+                                   slot_token=slot_token.data_ptr())
+        _lib.call("ic_tier_fill", a)
+        keep = []
+        for li in range(min(cfg.num_layers, len(pkv))):
+            K, V = pkv[li]
+            Ks = K[0].to(self.device)
+            Vs = V[0].to(self.device)
+            if Ks.stride(-1) != 1 or Vs.stride(-1) != 1 or Ks.stride() != Vs.stride():
+                Ks, Vs = Ks.contiguous(), Vs.contiguous()
+            src_dt = _lib.dtype_code(Ks.dtype)
+            Vs = Vs.to(Ks.dtype)
+            la = _lib.ic_load_layer_args(pool=self._c_pool, tiers=self._c_tiers, sess=sub, session=0, layer=li,
+                                         slot_token=slot_token.data_ptr(), k_src=Ks.data_ptr(), v_src=Vs.data_ptr(),
+                                         stride_h=Ks.stride(0), stride_t=Ks.stride(1), src_dtype=src_dt, T=T)
+            _lib.call("ic_load_layer", la)
+            keep.append((Ks, Vs))
+        self._keep = (keep, scores, pos, slot_token)
+        return slot_token
+
+    def _sort(self, sub=None):
+        sub = sub if sub is not None else self._c_sess
+        n = sub.num_sessions
+        srt = torch.empty((n, self.cfg.total_budget), dtype=torch.int32, device=self.device)
+        fill = torch.empty(n, dtype=torch.int32, device=self.device)
+        _lib.call("ic_sort_slots", _lib.ic_sort_args(tiers=self._c_tiers, sess=sub, sorted_slots=srt.data_ptr(),
+                                                     fill=fill.data_ptr()))
+        return srt, fill
+
+    def sorted_slots(self, session: int) -> torch.Tensor:
+        """Occupied slots of `session` in position order (int64, on device)."""
+        srt, fill = self._sort(self._sub(session))
+        return srt[0, : int(fill[0].item())].long()
+
+    def gather(self, session: int, slots: Optional[torch.Tensor] = None, layers: Optional[Tuple[int, int]] = None):
+        """K, V [L', Hkv, n, D] of `slots` (default: occupied slots in position
+        order) of one session."""
+        cfg = self.cfg
+        if slots is None:
+            slots = self.sorted_slots(session)
+        sl = slots.to(self.device, torch.int32).contiguous()
+        lb, le = layers if layers is not None else (0, cfg.num_layers)
+        n = sl.numel()
+        K = torch.empty((le - lb, cfg.num_kv_heads, n, cfg.head_dim), dtype=cfg.dtype, device=self.device)
+        V = torch.empty_like(K)
+        if n:
+            a = _lib.ic_gather_args(pool=self._c_pool, tiers=self._c_tiers, sess=self._c_sess, session=session, n=n,
+                                    slots=sl.data_ptr(), layer_begin=lb, layer_end=le, k_out=K.data_ptr(),
+                                    v_out=V.data_ptr())
+            _lib.call("ic_gather_slots", a)
+        return K, V
+
+    def reset(self, sessions: Optional[Sequence[int]] = None, zero_kv: bool = True) -> None:
+        if sessions is None:
+            sessions = range(self.num_sessions)
+        for s in sessions:
+            a = _lib.ic_reset_args(pool=self._c_pool, tiers=self._c_tiers, sess=self._c_sess, session0=int(s), n=1,
+                                   zero_kv=1 if zero_kv else 0)
+            _lib.call("ic_reset_sessions", a)
+
+    # ---- host views -----------------------------------------------------------------------------
+    def _sub(self, s: int) -> _lib.ic_sessions:
+        """ic_sessions for the single session row s."""
+        if not 0 <= s < self.num_sessions:
+            raise IndexError(s)
+        B = self.cfg.total_budget
+        return _lib.ic_sessions(num_sessions=1, slot_table=self.slot_table[s].data_ptr(),
+                                positions=self.positions[s].data_ptr(), importance=self.importance[s].data_ptr(),
+                                occupied=self.occupied[s].data_ptr(), ctrl=self.ctrl[s].data_ptr(),
+                                counters=self.counters[s].data_ptr(), dev_status=self.dev_status.data_ptr())
+
+    def stats(self, session: int) -> CacheStats:
+        c = self.ctrl[session].tolist()
+        n = self.counters[session].tolist()
+        sf, rf, imf = c[_lib.IC_CTRL_SINK_FILL], c[_lib.IC_CTRL_RECENT_FILL], c[_lib.IC_CTRL_IMPORTANT_FILL]
+        return CacheStats(total_tokens_seen=n[_lib.IC_CNT_TOKENS_SEEN], total_evictions=n[_lib.IC_CNT_EVICTIONS],
+                          current_fill=sf + rf + imf, sink_fill=sf, recent_fill=rf, important_fill=imf)
+
+    def check_device_status(self) -> None:
+        """Raise if a kernel reported a bounded-wait timeout or a bad row."""
+        st = int(self.dev_status.item())
+        if st & _lib.IC_DEVFLAG_TIMEOUT:
+            raise _lib.InferCacheError(_lib.IC_ERR_DEVICE_TIMEOUT, "a device-side wait timed out")
+        if st & _lib.IC_DEVFLAG_BAD_ROW:
+            raise _lib.InferCacheError(_lib.IC_ERR_CORRUPT_TABLE, "slot table or ring state out of range")
+
+
+class HierarchicalKVCache:
+    """Single-session drop-in for the reference class (hierarchical_cache.py:109-477)."""
+
+    def __init__(self, cfg: CacheConfig, device=None):
+        self.cfg = cfg
+        self.device = torch.device(device) if device is not None else torch.device("cuda")
+        if self.device.type != "cuda":
+            raise ValueError("HierarchicalKVCache runs on the GPU only (no CPU path)")
+        self._b = SessionBatch(cfg, 1, self.device)
+        self.device = self._b.device
+
+    # public tensors of the reference, device-resident views of session 0
+    @property
+    def positions(self) -> torch.Tensor:
+        return self._b.positions[0]
+
+    @property
+    def importance(self) -> torch.Tensor:
+        return self._b.importance[0]
+
+    @property
+    def occupied(self) -> torch.Tensor:
+        return self._b.occupied[0]
+
+    @property
+    def K(self) -> torch.Tensor:
+        """[L, Hkv, budget, D] by logical slot (a gathered copy)."""
+        return self._b.gather(0, torch.arange(self.cfg.total_budget, device=self.device))[0]
+
+    @property
+    def V(self) -> torch.Tensor:
+        return self._b.gather(0, torch.arange(self.cfg.total_budget, device=self.device))[1]
+
+    @property
+    def batch(self) -> SessionBatch:
+        return self._b
+
+    @property
+    def total_budget(self) -> int:
+        return self.cfg.total_budget
+
+    @property
+    def current_fill(self) -> int:
+        return self.stats.current_fill
+
+    @property
+    def stats(self) -> CacheStats:
+        return self._b.stats(0)
+
+    @property
+    def _recent_ptr(self) -> int:
+        return int(self._b.ctrl[0, _lib.IC_CTRL_RECENT_PTR].item())
+
+    @property
+    def _important_fill(self) -> int:
+        return int(self._b.ctrl[0, _lib.IC_CTRL_IMPORTANT_FILL].item())
+
+    def last_event(self) -> Tuple[int, int, int, int]:
+        """(kind, displaced position, target slot, evicted position) of the last push."""
+        return tuple(self._b.events[0].tolist())
+
+    def load_from_hf_output(self, past_key_values, importance_scores: torch.Tensor,
+                            positions: Optional[torch.Tensor] = None) -> None:
+        self._b.load_prompt(0, past_key_values, importance_scores, positions)
+
+    def push(self, key_states: torch.Tensor, value_states: torch.Tensor, position: int,
+             attn_weights: Optional[torch.Tensor] = None) -> None:
+        self._b.push(0, key_states, value_states, position, attn_weights)
+
+    # fused decode verbs for one session
+    def attend(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """q [Hq, D], k / v [Hkv, D] -> o [Hq, D]."""
+        return self._b.attend(layer, q[None], k[None], v[None], out_dtype=out_dtype)[0]
+
+    def evict(self, position: int, decay: Optional[float] = None) -> None:
+        self._b.evict([position], decay)
+
+    def step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, position: int,
+             out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+        """q [L, Hq, D], k / v [L, Hkv, D] -> o [L, Hq, D]."""
+        return self._b.step(q[:, None], k[:, None], v[:, None], [position], out_dtype=out_dtype)[:, 0]
+
+    def to_hf_past_key_values(self, device: Optional[torch.device] = None):
+        """Occupied slots in position order, one (K, V) [1, Hkv, F, D] per layer
+        (hierarchical_cache.py:297-351); None when empty."""
+        slots = self._b.sorted_slots(0)
+        if slots.numel() == 0:
+            return None
+        K, V = self._b.gather(0, slots)
+        dev = device or self.device
+        layers = [(K[l][None].to(dev), V[l][None].to(dev)) for l in range(self.cfg.num_layers)]
+        return to_dynamic_cache(layers)
+
+    def get_position_ids_for_cache(self) -> torch.Tensor:
+        slots = self._b.sorted_slots(0)
+        return self.positions[slots]
+
+    def reset(self) -> None:
+        self._b.reset([0], zero_kv=True)
+
+
+def _normalise_past_kv(past_key_values):
+    return normalise_kv(past_key_values)

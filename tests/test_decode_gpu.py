@@ -1,0 +1,344 @@
+"""Parity of the CUDA decode path (kernels A and B, tier fill, gathers) with
+the oracle and with the reference's golden fixtures.  Every call goes
+through the C ABI via the package's classes."""
+import numpy as np
+import pytest
+import torch
+
+import specs
+from gpu_protocol import compare_state, make_gpu_cache, run_c1, run_small
+from oracle.hier_cache import OracleCache, TierGeometry, decode_step
+from oracle.summary import tier_fill
+from tolerances import elem_close, rows_close, rows_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    torch.cuda.set_device(0)
+
+
+def test_c1_full_protocol(golden):
+    """4096-token single-layer fp32 decode: every step's output within 1e-5
+    of the oracle, every push event identical, final slot state identical;
+    and the same against the reference's own run."""
+    cache, oc, events, keep, worst = run_c1(check_every=512)
+    g = golden("c1_decode")
+    assert np.array_equal(events, g["events"])
+    assert cache.stats.total_evictions == 801
+    pos = cache.positions.cpu().numpy()
+    assert np.array_equal(pos, g["positions"])
+    assert np.array_equal(cache.occupied.cpu().numpy(), g["occupied"])
+    assert elem_close(cache.importance.cpu().numpy(), g["importance"], 1e-5)
+    for i, s in enumerate(g["keep_steps"]):
+        assert rows_close(keep[int(s)], g["o_keep"][i], 1e-5), s
+    assert worst < 1e-5
+    cache.batch.check_device_status()
+
+
+@pytest.mark.parametrize("name", list(specs.SMALL))
+def test_small_protocol(golden, name):
+    """Primed multi-layer decode (fp32, fp16, GQA 7:1, short prompt)."""
+    cache, oc, outs, events = run_small(name)
+    g = golden(f"small_decode_{name}")
+    rtol = 1e-5 if specs.SMALL[name]["dtype"] == "float32" else 1e-3
+    assert np.array_equal(events, g["events"])
+    assert rows_close(outs, g["o"], rtol)
+    assert np.array_equal(cache.positions.cpu().numpy(), g["positions"])
+    cache.batch.check_device_status()
+
+
+@pytest.mark.parametrize("name", list(specs.TIER))
+def test_tier_fill_exact(golden, name):
+    """load_from_hf_output slot placement is bit-exact with the reference."""
+    sp = specs.TIER[name]
+    g = golden(f"tier_fill_{name}")
+    scores, positions = specs.tier_inputs(name)
+    T = scores.shape[0]
+    cache = make_gpu_cache(1, 1, 128, sp["sink"], sp["recent"], sp["important"], torch.float32)
+    # K row of token t holds t, so the slot -> token map can be read back
+    kk = torch.arange(T, dtype=torch.float32)[None, None, :, None].expand(1, 1, T, 128).contiguous()
+    cache.load_from_hf_output(((kk, kk),), scores, positions=positions)
+    assert np.array_equal(cache.positions.cpu().numpy(), g["positions"])
+    assert np.array_equal(cache.importance.cpu().numpy(), g["importance"])
+    assert np.array_equal(cache.occupied.cpu().numpy(), g["occupied"])
+    Kl = cache.K[0, 0, :, 0].cpu()
+    tok = torch.where(cache.occupied.cpu(), Kl.long(), torch.full_like(Kl.long(), -1))
+    assert np.array_equal(tok.numpy(), g["slot_token"])
+    st = cache.stats
+    assert [st.sink_fill, st.recent_fill, cache._recent_ptr, st.important_fill] == list(g["fills"])
+    assert [st.total_tokens_seen, st.total_evictions] == list(g["counters"])
+
+
+def test_tier_fill_batch_random_ties():
+    """Many sessions primed at once, heavy ties, vs the oracle tier fill."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    from infercache_b200 import _lib
+    cfg = CacheConfig(num_layers=1, num_kv_heads=1, head_dim=128, sink_size=4, recent_size=64,
+                      important_size=300, dtype=torch.float16)
+    S, T = 12, 3000
+    b = SessionBatch(cfg, S, "cuda:0")
+    g = torch.Generator().manual_seed(21)
+    scores = (torch.rand(S, T, generator=g) * 50).round() / 50
+    positions = torch.stack([torch.randperm(T + 500, generator=g)[:T] for _ in range(S)])
+    slot_token = torch.empty((S, cfg.total_budget), dtype=torch.int32, device="cuda")
+    sc, ps = scores.cuda().contiguous(), positions.cuda().contiguous()
+    a = _lib.ic_tier_fill_args(tiers=b._c_tiers, sess=b._c_sess, session0=0, n=S, T=T, scores=sc.data_ptr(),
+                               positions=ps.data_ptr(), slot_token=slot_token.data_ptr())
+    _lib.call("ic_tier_fill", a)
+    st = slot_token.cpu().numpy()
+    for s in range(S):
+        r = tier_fill(scores[s].numpy(), positions[s].numpy(), 4, 64, 300)
+        assert np.array_equal(st[s], r["slot_token"]), s
+        assert np.array_equal(b.positions[s].cpu().numpy(), r["positions"]), s
+        assert int(b.counters[s, 1]) == r["counters"][1]
+
+
+def test_batch_sessions_vs_oracle():
+    """Several sessions in one launch, each checked against its own oracle."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    L, Hq, Hkv, D = 2, 16, 2, 128
+    sink, recent, imp = 4, 16, 12
+    S, T0, steps = 5, 60, 90
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=sink, recent_size=recent,
+                      important_size=imp, decay=0.99, dtype=torch.float16)
+    b = SessionBatch(cfg, S, "cuda:0")
+    geo = TierGeometry(L, Hkv, D, sink, recent, imp)
+    g = torch.Generator().manual_seed(5)
+    ocs = []
+    for s in range(S):
+        T = T0 + 7 * s
+        pk = torch.randn(L, Hkv, T, D, generator=g).half()
+        pv = torch.randn(L, Hkv, T, D, generator=g).half()
+        sc = torch.rand(T, generator=g)
+        b.load_prompt(s, tuple((pk[l][None], pv[l][None]) for l in range(L)), sc)
+        oc = OracleCache(geo, np.float16)
+        oc.load_from_hf_output(pk.float().numpy(), pv.float().numpy(), sc.numpy())
+        ocs.append((oc, T))
+    q = torch.randn(steps, L, S, Hq, D, generator=g).half()
+    k = torch.randn(steps, L, S, Hkv, D, generator=g).half()
+    v = torch.randn(steps, L, S, Hkv, D, generator=g).half()
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    for t in range(steps):
+        pos = torch.tensor([ocs[s][1] + t for s in range(S)], dtype=torch.int64, device="cuda")
+        o = b.step(qd[t], kd[t], vd[t], pos, out_dtype=torch.float32).cpu().numpy()
+        ev = b.events.cpu().numpy()
+        for s in range(S):
+            oc, T = ocs[s]
+            oo, e = decode_step(oc, q[t, :, s].float().numpy(), k[t, :, s].float().numpy(),
+                                v[t, :, s].float().numpy(), T + t, 0.99)
+            assert rows_close(o[:, s], oo, 1e-3), (t, s, rows_err(o[:, s], oo))
+            assert tuple(ev[s]) == e.as_tuple(), (t, s)
+    for s in range(S):
+        oc, _ = ocs[s]
+        assert np.array_equal(b.positions[s].cpu().numpy(), oc.positions)
+        assert elem_close(b.importance[s].cpu().numpy(), oc.importance, 1e-3)
+    b.check_device_status()
+
+
+def test_config2_full_size():
+    """The bench workload at full size: 36 layers, 16 sessions, 16/2 heads,
+    budget 4/256/780, fp16, 2048-token prompts.  Session 0 is checked against
+    the oracle step by step; all sessions are checked for invariants; a second
+    run from the same state reproduces every output bit for bit."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    L, Hq, Hkv, D, S, T, steps = 36, 16, 2, 128, 16, 2048, 6
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=4, recent_size=256,
+                      important_size=780, decay=0.99, dtype=torch.float16)
+    g = torch.Generator().manual_seed(1)
+    prompts = []
+
+    def build():
+        b = SessionBatch(cfg, S, "cuda:0")
+        for s in range(S):
+            b.load_prompt(s, tuple((prompts[s][0][l][None].cuda(), prompts[s][1][l][None].cuda())
+                                   for l in range(L)), prompts[s][2])
+        return b
+
+    for s in range(S):
+        prompts.append((torch.randn(L, Hkv, T, D, generator=g).half(), torch.randn(L, Hkv, T, D, generator=g).half(),
+                        torch.rand(T, generator=g)))
+    q = torch.randn(steps, L, S, Hq, D, generator=g).half()
+    k = torch.randn(steps, L, S, Hkv, D, generator=g).half()
+    v = torch.randn(steps, L, S, Hkv, D, generator=g).half()
+    b1 = build()
+    oc = OracleCache(TierGeometry(L, Hkv, D, 4, 256, 780), np.float16)
+    oc.load_from_hf_output(prompts[0][0].float().numpy(), prompts[0][1].float().numpy(), prompts[0][2].numpy())
+    outs = []
+    for t in range(steps):
+        o = b1.step(q[t].cuda(), k[t].cuda(), v[t].cuda(), [T + t] * S)
+        outs.append(o.clone())
+        oo, e = decode_step(oc, q[t, :, 0].float().numpy(), k[t, :, 0].float().numpy(),
+                            v[t, :, 0].float().numpy(), T + t, 0.99)
+        assert rows_close(o[:, 0].float().cpu().numpy(), oo, 1e-3), t
+        assert tuple(b1.events[0].tolist()) == e.as_tuple(), t
+    assert np.array_equal(b1.positions[0].cpu().numpy(), oc.positions)
+    # invariants on every session
+    ntot = cfg.total_budget + 1
+    for s in range(S):
+        rows = b1.slot_table[s].cpu()
+        assert rows.unique().numel() == ntot, "slot table is no longer a permutation of the session's rows"
+        pos = b1.positions[s].cpu()
+        assert bool(b1.occupied[s].all())
+        ring = pos[4:260]
+        assert sorted(ring.tolist())[-steps:] == [T + t for t in range(steps)]
+        assert pos.unique().numel() == cfg.total_budget
+        assert bool((b1.importance[s] >= 0).all())
+    # determinism
+    b2 = build()
+    for t in range(steps):
+        o = b2.step(q[t].cuda(), k[t].cuda(), v[t].cuda(), [T + t] * S)
+        assert torch.equal(o, outs[t]), t
+    assert torch.equal(b1.importance, b2.importance)
+    assert torch.equal(b1.slot_table, b2.slot_table)
+    b1.check_device_status()
+
+
+def test_cluster_sizes_agree():
+    """8- and 16-CTA clusters differ only in float summation order."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    cfg = CacheConfig(num_layers=2, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=256,
+                      important_size=780, dtype=torch.float16)
+    g = torch.Generator().manual_seed(3)
+    T = 1500
+    pk = torch.randn(2, 2, T, 128, generator=g).half()
+    sc = torch.rand(T, generator=g)
+    q = torch.randn(2, 3, 16, 128, generator=g).half().cuda()
+    kv = torch.randn(2, 3, 2, 128, generator=g).half().cuda()
+    res = []
+    for cl in (8, 16):
+        b = SessionBatch(cfg, 3, "cuda:0")
+        b.cluster_size = cl
+        for s in range(3):
+            b.load_prompt(s, tuple((pk[l][None], pk[l][None]) for l in range(2)), sc)
+        o = b.step(q, kv, kv, [T] * 3, out_dtype=torch.float32)
+        res.append((o.cpu().numpy(), b.events.cpu().numpy(), b.importance.cpu().numpy()))
+    assert rows_close(res[0][0], res[1][0], 1e-5)
+    assert np.array_equal(res[0][1], res[1][1])
+    assert elem_close(res[0][2], res[1][2], 1e-5)
+
+
+def test_push_reference_path():
+    """The reference-compatible push(key, value, position, attn_weights): mean
+    over (layers, heads, queries) added in position order, no decay."""
+    L, Hkv, D = 2, 2, 128
+    cache = make_gpu_cache(L, Hkv, D, 2, 5, 4, torch.float32)
+    geo = TierGeometry(L, Hkv, D, 2, 5, 4)
+    oc = OracleCache(geo, np.float32)
+    g = torch.Generator().manual_seed(11)
+    T = 14
+    pk = torch.randn(L, Hkv, T, D, generator=g)
+    sc = torch.rand(T, generator=g)
+    cache.load_from_hf_output(tuple((pk[l][None], pk[l][None]) for l in range(L)), sc)
+    oc.load_from_hf_output(pk.numpy(), pk.numpy(), sc.numpy())
+    for t in range(40):
+        kk = torch.randn(L, Hkv, 1, D, generator=g)
+        F = int(cache.occupied.sum())
+        w = None
+        if t % 5 != 4:   # every fifth push carries no weights (the shipped two_pass loop)
+            w = torch.rand(L, Hkv, 2, F + (t % 3) - 1, generator=g)  # widths F-1, F, F+1
+        cache.push(kk, kk, position=T + t, attn_weights=w)
+        e = oc.push(kk[:, :, 0].numpy(), kk[:, :, 0].numpy(), T + t, None if w is None else w.numpy())
+        assert cache.last_event() == e.as_tuple(), t
+        compare_state(cache, oc, 1e-6, f"push {t}")
+    # to_hf export and position ids
+    hf = cache.to_hf_past_key_values()
+    ref = oc.to_hf_past_key_values()
+    from infercache_b200.cache_safety import normalise_kv
+    for (K, V), (Ko, Vo) in zip(normalise_kv(hf), ref):
+        assert np.array_equal(K.cpu().numpy(), Ko)
+        assert np.array_equal(V.cpu().numpy(), Vo)
+    assert np.array_equal(cache.get_position_ids_for_cache().cpu().numpy(), oc.get_position_ids_for_cache())
+    cache.reset()
+    assert cache.current_fill == 0 and not bool(cache.occupied.any())
+    assert float(cache.K.abs().sum()) == 0.0
+
+
+def test_evict_kernel_ties_exact():
+    """Kernel B alone on crafted scores: equal minima are evicted lowest slot
+    first, a displaced score equal to the minimum is rejected, and the update
+    is importance * decay + mass / div with each step rounded."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    from infercache_b200 import _lib
+    cfg = CacheConfig(num_layers=3, num_kv_heads=2, head_dim=128, sink_size=2, recent_size=3,
+                      important_size=6, decay=0.5, dtype=torch.float16)
+    b = SessionBatch(cfg, 2, "cuda:0")
+    B = cfg.total_budget
+    # session 0: L2 full with a tied minimum at slots 7 and 9; ring slot 2 holds score 3
+    imp = torch.tensor([[9., 9., 3., 5., 5., 8., 4., 2., 6., 2., 7.],
+                        [9., 9., 1., 5., 5., 8., 4., 2., 6., 2., 7.]])
+    b.importance.copy_(imp)
+    b.occupied.fill_(True)
+    b.positions.copy_(torch.arange(B).repeat(2, 1) + 100)
+    b.ctrl[:, _lib.IC_CTRL_RECENT_FILL] = 3
+    b.ctrl[:, _lib.IC_CTRL_IMPORTANT_FILL] = 6
+    b.ctrl[:, _lib.IC_CTRL_RECENT_PTR] = 2
+    b.mass.zero_()
+    b.mass[1, :, 2] = 0.0
+    rows0 = b.slot_table.clone()
+    b.evict([500, 501], decay=1.0)
+    ev = b.events.cpu().tolist()
+    # session 0: score 3 > min 2 at slot 7 (first of the tie) -> evict slot 7
+    assert ev[0] == [3, 102, 7, 107]
+    # session 1: score 1 <= min 2 -> reject, target is still the first minimum
+    assert ev[1] == [4, 102, 7, -1]
+    st = b.slot_table.cpu()
+    assert st[0, 7] == rows0[0, 2] and st[0, 2] == rows0[0, B] and st[0, B] == rows0[0, 7]
+    assert st[1, 2] == rows0[1, B] and st[1, B] == rows0[1, 2]
+    assert b.positions[0, 2].item() == 500 and b.positions[0, 7].item() == 102
+    # decay + mass arithmetic on one session, rounded step by step
+    g = torch.Generator().manual_seed(2)
+    m = torch.rand(2, 2, B + 1, generator=g)
+    b.mass.copy_(m)
+    before = b.importance.clone()
+    b.evict([600, 601], decay=0.75)
+    want = (before.cpu().numpy() * np.float32(0.75)).astype(np.float32) + \
+           ((m[:, 0, :B].numpy() + m[:, 1, :B].numpy()) / np.float32(6.0)).astype(np.float32)
+    got = b.importance.cpu().numpy()
+    ev2 = b.events.cpu().numpy()
+    mask = np.ones_like(got, bool)
+    for s in range(2):
+        mask[s, 3] = False  # slot 3 is the new ring slot of this step (reset to 0)
+        if ev2[s, 0] in (2, 3):  # promotion target now holds the displaced score
+            mask[s, ev2[s, 2]] = False
+            assert got[s, ev2[s, 2]] == want[s, 3]
+    assert np.array_equal(got[mask], want.astype(np.float32)[mask])
+
+
+def test_paged_trace_gpu(golden):
+    """MultiSessionCache / KVAllocator / PagePool against the reference trace."""
+    import json
+    from infercache_b200 import MultiSessionCache, PagePool, PagedCacheConfig
+    sp = specs.PAGED
+    g = golden("paged_trace")
+    ticks = iter(range(1, 10 ** 6))
+    cfg = PagedCacheConfig(n_pages=sp["n_pages"], n_layers=sp["layers"], n_heads=sp["heads"], head_dim=sp["d"],
+                           dtype=torch.float32, device="cuda:0", max_pages_per_session=sp["max_pps"])
+    msc = MultiSessionCache(PagePool(cfg), clock=lambda: float(next(ticks)))
+    gathers = []
+    for i, op in enumerate(specs.paged_ops()):
+        err = ""
+        try:
+            if op[0] == "push":
+                _, sid, n, seed = op
+                kk, vv = specs.paged_tokens(n, seed)
+                view = msc.get_or_create(sid)
+                view.push(kk, vv, positions=list(range(view.n_tokens, view.n_tokens + n)),
+                          importance=[float(x) for x in np.linspace(0, 1, n)])
+            elif op[0] == "gather":
+                K, V = msc.get_or_create(op[1]).gather(op[2])
+                gathers.append(np.concatenate([K.cpu().numpy().ravel(), V.cpu().numpy().ravel()]))
+            elif op[0] == "reset":
+                msc.reset(op[1])
+            elif op[0] == "touch":
+                msc._alloc.touch(op[1])
+        except RuntimeError as e:
+            err = str(e)
+        assert err == str(g["errors"][i]), (i, op)
+        pages = {s: msc._alloc.pages_for(s) for s in sorted(msc.active_sessions())}
+        assert pages == json.loads(str(g["pages"][i])), (i, op)
+        assert abs(msc.utilization() - float(g["util"][i])) < 1e-12
+    assert np.array_equal(np.concatenate(gathers), g["gathers"])
