@@ -21,6 +21,7 @@ oracle restatement, one process per core) on the same workload.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import os
 import statistics
@@ -45,6 +46,11 @@ ALG_BYTES_PER_SESSION_LAYER = 1_082_756
 PROFILE_TRAFFIC = ROOT / "profiles" / "decode_layer_c2.md"
 
 
+def log(msg):
+    if os.environ.get("BENCH_VERBOSE"):
+        print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -61,16 +67,23 @@ class ClockSampler(threading.Thread):
         self.period = period_s
         self.samples = []
         self.reasons = 0
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self.ok = False
         try:
             import pynvml
             pynvml.nvmlInit()
             self.nv = pynvml
-            try:
-                bus = torch.cuda.get_device_properties(device_index).pci_bus_id
-                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            except Exception:
+            # match the CUDA device to its NVML handle by UUID
+            want = str(torch.cuda.get_device_properties(device_index).uuid).lower().replace("gpu-", "")
+            self.h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = (u.decode() if isinstance(u, bytes) else u).lower().replace("gpu-", "")
+                if u == want:
+                    self.h = h
+                    break
+            if self.h is None:
                 self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
             self.ok = True
@@ -78,7 +91,7 @@ class ClockSampler(threading.Thread):
             self.err = str(e)
 
     def run(self):
-        while self.ok and not self._stop.is_set():
+        while self.ok and not self._halt.is_set():
             try:
                 self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
                 self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
@@ -87,7 +100,7 @@ class ClockSampler(threading.Thread):
             time.sleep(self.period)
 
     def stop(self):
-        self._stop.set()
+        self._halt.set()
         if self.is_alive():
             self.join(timeout=2)
 
@@ -194,7 +207,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cluster", type=int, default=0)
+    ap.add_argument("--no-graph", action="store_true", help="replay steps eagerly instead of as a CUDA graph")
+    ap.add_argument("--no-clocks", action="store_true")
     args = ap.parse_args()
+    faulthandler.enable()
     args.warmup = max(3, args.warmup)
     rank, world, local_rank = dist_env()
 
@@ -211,6 +227,7 @@ def main():
 
     spec = dict(WORKLOAD)
     S, L, Hq, Hkv, D = spec["sessions"], spec["layers"], spec["hq"], spec["hkv"], spec["d"]
+    log("priming sessions")
     b = build_batch(spec, device, seed=1234 + rank)
     b.cluster_size = args.cluster
     g = torch.Generator(device=device).manual_seed(99 + rank)
@@ -232,50 +249,68 @@ def main():
         return float(t.item())
 
     # eager warm-up (also configures the kernels before capture)
+    log("warm-up")
     for _ in range(args.warmup):
         b.step(q, k, v, pos, out=out)
         pos.add_(1)
     torch.cuda.synchronize()
 
-    # one decode step of every session, captured once and replayed
-    cap = torch.cuda.Stream()
-    cap.wait_stream(torch.cuda.current_stream())
-    step_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(step_graph, stream=cap):
+    def eager_step():
         b.step(q, k, v, pos, out=out)
         pos.add_(1)
-    dec_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(dec_graph, stream=cap):
+
+    def eager_dec():
         for l in range(L):
             b.attend(l, q[l], k[l], v[l], out=out[l])
+
+    run_step, run_dec = eager_step, eager_dec
+    graphs = []
+    if not args.no_graph:
+        # one decode step of every session, captured once and replayed
+        log("capture")
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(step_graph, stream=cap):
+            eager_step()
+        dec_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(dec_graph, stream=cap):
+            eager_dec()
+        graphs = [step_graph, dec_graph]
+        run_step, run_dec = step_graph.replay, dec_graph.replay
+    log("graph warm-up")
     for _ in range(args.warmup):
-        step_graph.replay()
+        run_step()
     torch.cuda.synchronize()
 
-    sampler = ClockSampler(local_rank)
-    sampler.start()
+    sampler = ClockSampler(local_rank) if not args.no_clocks else None
+    if sampler:
+        sampler.start()
+    log("timed region")
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        step_graph.replay()
+        run_step()
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    sampler.stop()
+    if sampler:
+        sampler.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
     value = world * S * args.steps / (ms / 1e3)
 
-    # decode-kernel launch duration for the roofline (graph of 36 launches)
+    # decode-kernel launch duration for the roofline (36 back-to-back launches)
+    log("decode-only timing")
     kd = max(10, min(args.steps, 300))
     for _ in range(3):
-        dec_graph.replay()
+        run_dec()
     torch.cuda.synchronize()
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0.record()
     for _ in range(kd):
-        dec_graph.replay()
+        run_dec()
     d1.record()
     torch.cuda.synchronize()
     dec_launch_s = max_over_ranks(d0.elapsed_time(d1)) / 1e3 / (kd * L)
@@ -285,6 +320,7 @@ def main():
     traffic = read_traffic()
 
     # end to end through the public API: pinned host inputs -> device -> step -> host outputs
+    log("e2e")
     qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
     oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     qd, kd_, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
@@ -329,10 +365,11 @@ def main():
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "steps": ke, "api": "SessionBatch.step (ic_decode_step) with pinned host buffers"},
                 "gpu_launches": args.steps * (L + 1),
-                "clocks": sampler.summary()}
+                "clocks": sampler.summary() if sampler else None,
+                "cuda_graph": not args.no_graph}
         print(json.dumps(line), flush=True)
     if world > 1:
-        del step_graph, dec_graph
+        del graphs
         dist.destroy_process_group()
 
 

@@ -140,7 +140,13 @@ typedef struct ic_decode_args {
   float* mass;             /* [S, Hkv, budget + 1] */
   float scale;             /* softmax scale, normally head_dim ** -0.5 */
   int32_t cluster_size;    /* 0 = choose; else 8 or 16 */
+  int32_t kernel_variant;  /* ic_decode_variant */
+  int32_t _pad2;
 } ic_decode_args;
+
+/* Kernel A implementations.  AUTO picks tensor cores for fp16 / bf16 pools
+ * and CUDA cores for fp32. */
+enum ic_decode_variant { IC_DECODE_AUTO = 0, IC_DECODE_CUDA_CORES = 1, IC_DECODE_TENSOR_CORES = 2 };
 int ic_decode_layer(const ic_decode_args* a, void* stream);
 
 /* ---- Kernel B: importance update, promotion / eviction, ring advance -----

@@ -35,6 +35,7 @@ IC_CNT_TOKENS_SEEN, IC_CNT_EVICTIONS, IC_CNT_STEPS, IC_CNT_PROMOTIONS = 0, 1, 2,
 IC_COUNTER_WORDS = 4
 IC_EV_NONE, IC_EV_DROP, IC_EV_FILL, IC_EV_EVICT, IC_EV_REJECT = 0, 1, 2, 3, 4
 IC_DEVFLAG_TIMEOUT, IC_DEVFLAG_BAD_ROW = 1, 2
+IC_DECODE_AUTO, IC_DECODE_CUDA_CORES, IC_DECODE_TENSOR_CORES = 0, 1, 2
 
 DTYPE_CODE = {torch.float32: IC_F32, torch.float16: IC_F16, torch.bfloat16: IC_BF16}
 
@@ -77,7 +78,7 @@ class ic_decode_args(Structure):
     _fields_ = [("pool", ic_pool), ("tiers", ic_tiers), ("sess", ic_sessions), ("layer", c_int32),
                 ("num_q_heads", c_int32), ("q", c_void_p), ("k_new", c_void_p), ("v_new", c_void_p),
                 ("out", c_void_p), ("out_dtype", c_int32), ("accumulate", c_int32), ("mass", c_void_p),
-                ("scale", c_float), ("cluster_size", c_int32)]
+                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("_pad2", c_int32)]
 
 
 class ic_evict_args(Structure):

@@ -20,6 +20,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "decode_internal.cuh"
 
 namespace ic {
 
@@ -353,6 +354,16 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
     return IC_ERR_INVALID_ARG;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int variant = a->kernel_variant;
+  if (variant != IC_DECODE_AUTO && variant != IC_DECODE_CUDA_CORES && variant != IC_DECODE_TENSOR_CORES) {
+    set_last_error("decode: bad kernel_variant");
+    return IC_ERR_INVALID_ARG;
+  }
+  if (a->pool.dtype != IC_F32 && variant != IC_DECODE_CUDA_CORES) return launch_decode_mma(*a, st);
+  if (a->pool.dtype == IC_F32 && variant == IC_DECODE_TENSOR_CORES) {
+    set_last_error("decode: the tensor-core variant needs an fp16 or bf16 pool");
+    return IC_ERR_UNSUPPORTED;
+  }
   switch (a->pool.dtype) {
     case IC_F32: return dispatch_gp<float>(*a, st);
     case IC_F16: return dispatch_gp<__half>(*a, st);

@@ -146,6 +146,7 @@ class SessionBatch:
         self._pos_buf = torch.zeros(S, dtype=torch.int64, device=dev)
         self.scale = cfg.head_dim ** -0.5
         self.cluster_size = 0
+        self.kernel_variant = _lib.IC_DECODE_AUTO
 
         self._c_tiers = _lib.ic_tiers(cfg.sink_size, cfg.recent_size, cfg.important_size, B)
         self._c_sess = _lib.ic_sessions(num_sessions=S, slot_table=self.slot_table.data_ptr(),
@@ -192,6 +193,7 @@ class SessionBatch:
         d.out_dtype = _lib.dtype_code(out.dtype)
         d.accumulate = 1 if layer > 0 else 0
         d.cluster_size = self.cluster_size
+        d.kernel_variant = self.kernel_variant
         _lib.call("ic_decode_layer", d)
         return out
 
@@ -237,6 +239,7 @@ class SessionBatch:
         d.out = out.data_ptr()
         d.out_dtype = _lib.dtype_code(out.dtype)
         d.cluster_size = self.cluster_size
+        d.kernel_variant = self.kernel_variant
         st.q_layer_stride = S * Hq * D
         st.kv_layer_stride = S * cfg.num_kv_heads * D
         st.out_layer_stride = S * Hq * D

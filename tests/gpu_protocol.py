@@ -69,16 +69,26 @@ def run_c1(steps=None, check_every=1):
     return cache, oc, np.array(events, np.int64), keep, worst
 
 
-def run_small(name, out_dtype=torch.float32):
-    """Primed multi-layer decode of one SMALL spec, GPU vs oracle per step."""
-    sp = specs.SMALL[name]
+def run_small(name, out_dtype=torch.float32, variant=0, dtype=None):
+    """Primed multi-layer decode of one SMALL spec, GPU vs oracle per step.
+
+    variant: kernel A implementation (0 auto, 1 CUDA cores, 2 tensor cores).
+    dtype: override the spec's cache dtype ("bfloat16": the oracle then holds
+    the bf16-rounded values in float32 storage, which is exact)."""
+    sp = dict(specs.SMALL[name])
+    base_dt = sp["dtype"]
+    if dtype is not None:
+        sp["dtype"] = dtype
     dt = TORCH_DT[sp["dtype"]]
     rtol = 1e-5 if sp["dtype"] == "float32" else 1e-3
     pk, pv, scores, q, k, v = specs.small_inputs(name)
+    if dtype is not None and dtype != base_dt:
+        pk, pv, q, k, v = (t.to(dt).float() for t in (pk, pv, q, k, v))
     cache = make_gpu_cache(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"], dt,
                            sp["decay"])
+    cache.batch.kernel_variant = variant
     geo = TierGeometry(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"])
-    oc = OracleCache(geo, NP_DT[sp["dtype"]])
+    oc = OracleCache(geo, NP_DT.get(sp["dtype"], np.float32))
     pkv = tuple((pk[l][None].to(dt), pv[l][None].to(dt)) for l in range(sp["layers"]))
     cache.load_from_hf_output(pkv, scores)
     oc.load_from_hf_output(pk.numpy(), pv.numpy(), scores.numpy())

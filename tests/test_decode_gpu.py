@@ -51,6 +51,21 @@ def test_small_protocol(golden, name):
     cache.batch.check_device_status()
 
 
+@pytest.mark.parametrize("name", ["f16", "g7"])
+@pytest.mark.parametrize("variant", [1, 2])
+def test_small_protocol_variants(name, variant):
+    """Both kernel-A implementations (CUDA cores, tensor cores) against the oracle."""
+    cache, oc, outs, events = run_small(name, variant=variant)
+    cache.batch.check_device_status()
+
+
+@pytest.mark.parametrize("name", ["f16", "g7", "short_prompt"])
+def test_small_protocol_bf16(name):
+    """bf16 caches (tensor-core kernel) against the oracle on bf16-rounded inputs."""
+    cache, oc, outs, events = run_small(name, dtype="bfloat16")
+    cache.batch.check_device_status()
+
+
 @pytest.mark.parametrize("name", list(specs.TIER))
 def test_tier_fill_exact(golden, name):
     """load_from_hf_output slot placement is bit-exact with the reference."""
