@@ -141,12 +141,16 @@ typedef struct ic_decode_args {
   float scale;             /* softmax scale, normally head_dim ** -0.5 */
   int32_t cluster_size;    /* 0 = choose; else 8 or 16 */
   int32_t kernel_variant;  /* ic_decode_variant */
-  int32_t _pad2;
+  int32_t pdl;             /* 1: launch with programmatic dependent launch */
 } ic_decode_args;
 
 /* Kernel A implementations.  AUTO picks tensor cores for fp16 / bf16 pools
  * and CUDA cores for fp32. */
-enum ic_decode_variant { IC_DECODE_AUTO = 0, IC_DECODE_CUDA_CORES = 1, IC_DECODE_TENSOR_CORES = 2 };
+enum ic_decode_variant {
+  IC_DECODE_AUTO = 0,
+  IC_DECODE_CUDA_CORES = 1,    /* fp32 / fp16 / bf16 */
+  IC_DECODE_TENSOR_CORES = 2   /* fp16 / bf16 */
+};
 int ic_decode_layer(const ic_decode_args* a, void* stream);
 
 /* ---- Kernel B: importance update, promotion / eviction, ring advance -----
@@ -166,7 +170,7 @@ typedef struct ic_evict_args {
   int32_t mass_rows;
   float mass_div;
   float decay;
-  int32_t _pad;
+  int32_t pdl;             /* 1: launch with programmatic dependent launch */
   const int64_t* new_pos;  /* [S] */
   int64_t* events;         /* [S, 4] record of this step, or NULL */
 } ic_evict_args;

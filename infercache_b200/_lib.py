@@ -78,12 +78,12 @@ class ic_decode_args(Structure):
     _fields_ = [("pool", ic_pool), ("tiers", ic_tiers), ("sess", ic_sessions), ("layer", c_int32),
                 ("num_q_heads", c_int32), ("q", c_void_p), ("k_new", c_void_p), ("v_new", c_void_p),
                 ("out", c_void_p), ("out_dtype", c_int32), ("accumulate", c_int32), ("mass", c_void_p),
-                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("_pad2", c_int32)]
+                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32)]
 
 
 class ic_evict_args(Structure):
     _fields_ = [("tiers", ic_tiers), ("sess", ic_sessions), ("mass", c_void_p), ("mass_rows", c_int32),
-                ("mass_div", c_float), ("decay", c_float), ("_pad", c_int32), ("new_pos", c_void_p),
+                ("mass_div", c_float), ("decay", c_float), ("pdl", c_int32), ("new_pos", c_void_p),
                 ("events", c_void_p)]
 
 

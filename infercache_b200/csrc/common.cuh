@@ -122,6 +122,58 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// ---- 16-byte asynchronous global -> shared copies (LDGSTS), L1 bypassed ------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- programmatic dependent launch ------------------------------------------------
+// Wait until the grids this one depends on have completed and their writes
+// are visible (returns at once when launched without the PDL attribute).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next grid in the stream to begin launching.
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---- cluster helpers ---------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Split cluster barrier: every thread of every CTA arrives, then waits.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Asynchronous stores into a (possibly remote) CTA's shared memory, completing
+// as transaction bytes on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_v2(uint32_t addr, uint32_t x, uint32_t y, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "r"(x), "r"(y), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint32_t x, uint32_t y, uint32_t z, uint32_t w,
+                                            uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+               : "memory");
+}
+
 // ---- warp reductions ---------------------------------------------------------
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -154,5 +206,19 @@ __device__ __forceinline__ void warp_argmin(float& v, int& i) {
 // ---- host-side status plumbing ----------------------------------------------
 void set_last_error(const char* msg);
 int launch_status(const char* what);
+
+// Raise a kernel's dynamic shared-memory limit to `bytes` if it is below it
+// (tracked per kernel in `*limit`).  Returns IC_OK or IC_ERR_UNSUPPORTED.
+template <typename F>
+inline int ensure_dynamic_smem(F* kernel, int bytes, int* limit) {
+  if (bytes <= 48 * 1024 || bytes <= *limit) return IC_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    set_last_error("kernel needs more shared memory than the device allows");
+    return IC_ERR_UNSUPPORTED;
+  }
+  *limit = bytes;
+  return IC_OK;
+}
 
 }  // namespace ic

@@ -276,10 +276,12 @@ static int launch_decode(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_UNSUPPORTED;
   }
   auto kern = decode_kernel<T, CL, GP>;
+  static int smem_limit = 0;
+  if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaGetLastError();
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -355,7 +357,7 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int variant = a->kernel_variant;
-  if (variant != IC_DECODE_AUTO && variant != IC_DECODE_CUDA_CORES && variant != IC_DECODE_TENSOR_CORES) {
+  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_CORES) {
     set_last_error("decode: bad kernel_variant");
     return IC_ERR_INVALID_ARG;
   }

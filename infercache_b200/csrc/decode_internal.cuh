@@ -7,7 +7,7 @@
 
 namespace ic {
 
-// Tensor-core variant of kernel A (fp16 / bf16 pools, head_dim 128).
+// Tensor-core kernel A, one cluster per (session, KV head) (fp16 / bf16).
 int launch_decode_mma(const ic_decode_args& a, cudaStream_t stream);
 
 }  // namespace ic

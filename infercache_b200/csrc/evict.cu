@@ -38,6 +38,11 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   int64_t* pos = a.sess.positions + static_cast<size_t>(s) * B;
   int32_t* stt = a.sess.slot_table + static_cast<size_t>(s) * ntot;
 
+  // launched with programmatic dependent launch: the last layer's mass must
+  // be complete before it is read; the next step's first layer waits for us
+  grid_dependency_wait();
+  grid_launch_dependents();
+
   // 1. decay + boost of every occupied slot
   const float decay = a.decay;
   const float div = a.mass_div;
@@ -281,12 +286,19 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
   }
   const size_t smem = static_cast<size_t>(a->tiers.budget) * sizeof(float);
   if (smem > 200 * 1024) { set_last_error("evict_update: budget too large"); return IC_ERR_UNSUPPORTED; }
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(evict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
-  }
-  evict_kernel<<<a->sess.num_sessions, EV_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(*a);
+  static int smem_limit = 0;
+  if (const int rc = ensure_dynamic_smem(evict_kernel, static_cast<int>(smem), &smem_limit)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a->sess.num_sessions, 1, 1);
+  cfg.blockDim = dim3(EV_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = a->pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, evict_kernel, *a);
   return launch_status("evict_update");
 }
 
@@ -299,11 +311,8 @@ extern "C" int ic_sort_slots(const ic_sort_args* a, void* stream) {
   }
   const size_t smem = static_cast<size_t>(a->tiers.budget) * 9;
   if (smem > 200 * 1024) { set_last_error("sort_slots: budget too large"); return IC_ERR_UNSUPPORTED; }
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(sort_slots_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
-  }
+  static int smem_limit = 0;
+  if (const int rc = ensure_dynamic_smem(sort_slots_kernel, static_cast<int>(smem), &smem_limit)) return rc;
   sort_slots_kernel<<<a->sess.num_sessions, SORT_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(*a);
   return launch_status("sort_slots");
 }

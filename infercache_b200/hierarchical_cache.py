@@ -160,6 +160,8 @@ class SessionBatch:
                                       mass_rows=cfg.num_kv_heads, mass_div=float(cfg.num_layers * cfg.num_kv_heads),
                                       decay=cfg.decay, new_pos=self._pos_buf.data_ptr(),
                                       events=self.events.data_ptr())
+        # programmatic dependent launch between the step's kernels
+        self.pdl = True
         self._step = _lib.ic_step_args(layer0=self._dec, evict=self._ev)
 
     # ---- hot path -------------------------------------------------------------------
@@ -184,18 +186,23 @@ class SessionBatch:
         elif out.shape != q.shape or not out.is_contiguous() or out.device != self.device:
             raise ValueError("out must be a contiguous [S, Hq, D] tensor on the cache device")
         d = self._dec
+        self._prepare_decode(d, Hq)
         d.layer = layer
-        d.num_q_heads = Hq
         d.q = q.data_ptr()
         d.k_new = k.data_ptr()
         d.v_new = v.data_ptr()
         d.out = out.data_ptr()
         d.out_dtype = _lib.dtype_code(out.dtype)
         d.accumulate = 1 if layer > 0 else 0
-        d.cluster_size = self.cluster_size
-        d.kernel_variant = self.kernel_variant
         _lib.call("ic_decode_layer", d)
         return out
+
+    def _prepare_decode(self, d: "_lib.ic_decode_args", Hq: int) -> None:
+        """Set the launch options of one decode call on `d`."""
+        d.num_q_heads = Hq
+        d.cluster_size = self.cluster_size
+        d.kernel_variant = self.kernel_variant
+        d.pdl = 1 if self.pdl else 0
 
     def evict(self, positions, decay: Optional[float] = None) -> None:
         """Kernel B once per step after the last layer.  positions: [S] int64
@@ -207,6 +214,7 @@ class SessionBatch:
         e.mass = self.mass.data_ptr()
         e.mass_rows = self.cfg.num_kv_heads
         e.mass_div = float(self.cfg.num_layers * self.cfg.num_kv_heads)
+        e.pdl = 1 if self.pdl else 0
         _lib.call("ic_evict_update", e)
         self._keep = pos  # keep alive until the launch is consumed
 
@@ -232,14 +240,13 @@ class SessionBatch:
         pos = self._positions_arg(positions)
         st = self._step
         d = st.layer0
-        d.num_q_heads = Hq
+        self._prepare_decode(d, Hq)
         d.q = q.data_ptr()
         d.k_new = k.data_ptr()
         d.v_new = v.data_ptr()
         d.out = out.data_ptr()
         d.out_dtype = _lib.dtype_code(out.dtype)
-        d.cluster_size = self.cluster_size
-        d.kernel_variant = self.kernel_variant
+        st.evict.pdl = 1 if self.pdl else 0
         st.q_layer_stride = S * Hq * D
         st.kv_layer_stride = S * cfg.num_kv_heads * D
         st.out_layer_stride = S * Hq * D
