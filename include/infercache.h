@@ -119,8 +119,9 @@ typedef struct ic_sessions {
  * staging row of layer `layer`, attends the Hq/Hkv query heads of the group
  * over every occupied logical slot plus the new token (scale * q.k, softmax,
  * P.V), writes out[s, h*G + g], and stores the received mass of each slot
- * summed over the group's query heads into mass[s, h, slot] (overwrite when
- * accumulate == 0, add when 1; index `budget` is the new token).
+ * summed over the group's query heads into mass[s, h, slot, layer] (index
+ * `budget` is the new token; the layer index is the innermost dimension, of
+ * size mass_layers).
  * Replaces: compact_sdp_attention (triton_ops.py:251-287), gather_cache_kv
  * (:107-135), scatter_importance (:148-175), the model attention fed by
  * to_hf_past_key_values (hierarchical_cache.py:297-351, two_pass.py:312-321)
@@ -136,27 +137,35 @@ typedef struct ic_decode_args {
   const void* v_new;       /* [S, Hkv, D] pool dtype */
   void* out;               /* [S, Hq, D]  out_dtype */
   int32_t out_dtype;       /* ic_dtype: pool dtype or IC_F32 */
-  int32_t accumulate;
-  float* mass;             /* [S, Hkv, budget + 1] */
+  int32_t inputs_ready;    /* 1: q, k_new and v_new of every layer of this
+                              step were complete before the step's first
+                              launch (ic_decode_step), so a layer may read them
+                              before the previous layer finishes; 0: they may
+                              come from the immediately preceding kernel */
+  float* mass;             /* [S, Hkv, budget + 1, mass_layers] */
   float scale;             /* softmax scale, normally head_dim ** -0.5 */
-  int32_t cluster_size;    /* 0 = choose; else 8 or 16 */
+  int32_t cluster_size;    /* cluster variant: 0 = choose; else 8 or 16 */
   int32_t kernel_variant;  /* ic_decode_variant */
   int32_t pdl;             /* 1: launch with programmatic dependent launch */
+  int32_t mass_layers;     /* innermost dimension of mass (>= layer + 1) */
 } ic_decode_args;
 
-/* Kernel A implementations.  AUTO picks tensor cores for fp16 / bf16 pools
- * and CUDA cores for fp32. */
+/* Kernel A implementations.  AUTO picks CUDA cores for fp32 pools; for fp16 /
+ * bf16 pools the streaming kernel when inputs_ready and pdl are set (the
+ * layers of one ic_decode_step overlap) and the cluster kernel otherwise. */
 enum ic_decode_variant {
   IC_DECODE_AUTO = 0,
-  IC_DECODE_CUDA_CORES = 1,    /* fp32 / fp16 / bf16 */
-  IC_DECODE_TENSOR_CORES = 2   /* fp16 / bf16 */
+  IC_DECODE_CUDA_CORES = 1,      /* fp32 / fp16 / bf16, one cluster per group   */
+  IC_DECODE_TENSOR_CORES = 2,    /* fp16 / bf16, one cluster per group          */
+  IC_DECODE_TENSOR_STREAM = 3    /* fp16 / bf16, one CTA streams a whole group  */
 };
 int ic_decode_layer(const ic_decode_args* a, void* stream);
 
 /* ---- Kernel B: importance update, promotion / eviction, ring advance -----
  * Once per session-step after the last layer.  For every occupied slot j:
- *   importance[j] = importance[j] * decay + (sum_r mass[s, r, j]) / mass_div
- * (decay == 1 leaves the product exact; mass == NULL adds nothing).  Then the
+ *   importance[j] = importance[j] * decay + (sum_h sum_l mass[s, h, j, l]) / mass_div
+ * (sums in index order, heads outer; decay == 1 leaves the product exact;
+ * mass == NULL adds nothing).  Then the
  * token in ring slot recent_ptr, if any, is promoted to L2 or dropped exactly
  * as _maybe_promote_to_l2 (hierarchical_cache.py:448-477) with the
  * first-index argmin of _l2_min_slot (:420-425), and the staging row becomes
@@ -166,8 +175,9 @@ int ic_decode_layer(const ic_decode_args* a, void* stream);
 typedef struct ic_evict_args {
   ic_tiers tiers;
   ic_sessions sess;
-  const float* mass;       /* [S, mass_rows, budget + 1] or NULL */
-  int32_t mass_rows;
+  const float* mass;       /* [S, mass_heads, budget + 1, mass_layers] or NULL */
+  int32_t mass_heads;
+  int32_t mass_layers;
   float mass_div;
   float decay;
   int32_t pdl;             /* 1: launch with programmatic dependent launch */
@@ -177,11 +187,12 @@ typedef struct ic_evict_args {
 int ic_evict_update(const ic_evict_args* a, void* stream);
 
 /* ---- One whole decode step: kernel A for layers 0 .. L-1, then kernel B ---
- * `layer0` describes layer 0 (its `layer` and `accumulate` fields are
+ * `layer0` describes layer 0 (its `layer` and `inputs_ready` fields are
  * ignored); layer l reads q + l * q_layer_stride, k_new / v_new +
  * l * kv_layer_stride and writes out + l * out_layer_stride (strides in
  * elements of the respective dtype).  `evict` is then applied with its own
- * fields (normally mass rows = Hkv, mass_div = L * Hkv).  The decode loop of
+ * fields (normally mass_heads = Hkv, mass_layers = L, mass_div = L * Hkv).
+ * Layers are launched with inputs_ready = 1.  The decode loop of
  * _generate_two_pass (two_pass.py:302-336) with the model's per-layer
  * attention and the cache push of one token per session. */
 typedef struct ic_step_args {
@@ -223,8 +234,9 @@ int ic_sort_slots(const ic_sort_args* a, void* stream);
 /* ---- Reference push boost: mean attention weight by position rank --------
  * weights: float [S, L, H, Q, width] (the attn_weights of push, per
  * session).  agg[r] = (sum_h sum_l sum_q w[l, h, q, r]) / (L * H * Q);
- * mass_out[s, 0, sorted_slots[s, r]] = agg[r] for r < min(width, fill),
- * 0 for every other slot (_boost_importance, hierarchical_cache.py:427-446). */
+ * mass_out[s, sorted_slots[s, r]] = agg[r] for r < min(width, fill), 0 for
+ * every other slot (_boost_importance, hierarchical_cache.py:427-446); use it
+ * as kernel B's mass with one head and one layer. */
 typedef struct ic_boost_args {
   ic_tiers tiers;
   int32_t num_sessions;
@@ -232,7 +244,7 @@ typedef struct ic_boost_args {
   const float* weights;
   const int32_t* sorted_slots;  /* from ic_sort_slots */
   const int32_t* fill;
-  float* mass_out;              /* [S, 1, budget + 1] */
+  float* mass_out;              /* [S, budget + 1] */
 } ic_boost_args;
 int ic_boost_sorted(const ic_boost_args* a, void* stream);
 

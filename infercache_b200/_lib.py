@@ -35,7 +35,7 @@ IC_CNT_TOKENS_SEEN, IC_CNT_EVICTIONS, IC_CNT_STEPS, IC_CNT_PROMOTIONS = 0, 1, 2,
 IC_COUNTER_WORDS = 4
 IC_EV_NONE, IC_EV_DROP, IC_EV_FILL, IC_EV_EVICT, IC_EV_REJECT = 0, 1, 2, 3, 4
 IC_DEVFLAG_TIMEOUT, IC_DEVFLAG_BAD_ROW = 1, 2
-IC_DECODE_AUTO, IC_DECODE_CUDA_CORES, IC_DECODE_TENSOR_CORES = 0, 1, 2
+IC_DECODE_AUTO, IC_DECODE_CUDA_CORES, IC_DECODE_TENSOR_CORES, IC_DECODE_TENSOR_STREAM = 0, 1, 2, 3
 
 DTYPE_CODE = {torch.float32: IC_F32, torch.float16: IC_F16, torch.bfloat16: IC_BF16}
 
@@ -77,14 +77,15 @@ class ic_sessions(Structure):
 class ic_decode_args(Structure):
     _fields_ = [("pool", ic_pool), ("tiers", ic_tiers), ("sess", ic_sessions), ("layer", c_int32),
                 ("num_q_heads", c_int32), ("q", c_void_p), ("k_new", c_void_p), ("v_new", c_void_p),
-                ("out", c_void_p), ("out_dtype", c_int32), ("accumulate", c_int32), ("mass", c_void_p),
-                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32)]
+                ("out", c_void_p), ("out_dtype", c_int32), ("inputs_ready", c_int32), ("mass", c_void_p),
+                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32),
+                ("mass_layers", c_int32)]
 
 
 class ic_evict_args(Structure):
-    _fields_ = [("tiers", ic_tiers), ("sess", ic_sessions), ("mass", c_void_p), ("mass_rows", c_int32),
-                ("mass_div", c_float), ("decay", c_float), ("pdl", c_int32), ("new_pos", c_void_p),
-                ("events", c_void_p)]
+    _fields_ = [("tiers", ic_tiers), ("sess", ic_sessions), ("mass", c_void_p), ("mass_heads", c_int32),
+                ("mass_layers", c_int32), ("mass_div", c_float), ("decay", c_float), ("pdl", c_int32),
+                ("new_pos", c_void_p), ("events", c_void_p)]
 
 
 class ic_step_args(Structure):

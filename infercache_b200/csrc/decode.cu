@@ -13,7 +13,7 @@
 //      cluster through distributed shared memory, so every probability is
 //      exp(s - m) / l with the exact global m and l;
 //   4. writes the received mass of each slot summed over the group's query
-//      heads (overwrite on the first layer of a step, accumulate after);
+//      heads into this layer's column of the mass array;
 //   5. computes its partial P.V and reduces the partials across the cluster
 //      through DSMEM in a fixed CTA order.
 // No global scratch, no atomics: results are deterministic run to run.
@@ -222,11 +222,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(const ic_decode_
 
   // -- 4. received mass per slot, summed over the group's heads in order -----
   {
-    float* mrow = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + t0;
+    const size_t ML = static_cast<size_t>(a.mass_layers);
+    float* mrow = a.mass + ((static_cast<size_t>(s) * Hkv + h) * ntot + t0) * ML + a.layer;
     for (int t = tid; t < n; t += DEC_THREADS) {
       float m = 0.f;
       for (int g = 0; g < G; ++g) m += sc[g * cp + t];
-      mrow[t] = a.accumulate ? mrow[t] + m : m;
+      mrow[static_cast<size_t>(t) * ML] = m;
     }
   }
 
@@ -347,6 +348,7 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   if (a->tiers.budget <= 0 || a->tiers.budget != a->tiers.sink_size + a->tiers.recent_size +
                                                      a->tiers.important_size ||
       a->layer < 0 || a->layer >= a->pool.num_layers || a->sess.num_sessions < 0 ||
+      a->mass_layers <= a->layer ||
       a->pool.pool_tokens <= 0 || a->sess.num_sessions > 65535 || Hkv > 65535) {
     set_last_error("decode: bad sizes");
     return IC_ERR_INVALID_ARG;
@@ -357,12 +359,18 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int variant = a->kernel_variant;
-  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_CORES) {
+  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_STREAM) {
     set_last_error("decode: bad kernel_variant");
     return IC_ERR_INVALID_ARG;
   }
+  // AUTO on fp16 / bf16: the streaming kernel when the step's inputs are all
+  // ready (consecutive layers then overlap), the cluster kernel otherwise
+  // (lowest latency for one layer at a time).
+  if (a->pool.dtype != IC_F32 &&
+      (variant == IC_DECODE_TENSOR_STREAM || (variant == IC_DECODE_AUTO && a->inputs_ready && a->pdl)))
+    return launch_decode_stream(*a, st);
   if (a->pool.dtype != IC_F32 && variant != IC_DECODE_CUDA_CORES) return launch_decode_mma(*a, st);
-  if (a->pool.dtype == IC_F32 && variant == IC_DECODE_TENSOR_CORES) {
+  if (a->pool.dtype == IC_F32 && variant >= IC_DECODE_TENSOR_CORES) {
     set_last_error("decode: the tensor-core variant needs an fp16 or bf16 pool");
     return IC_ERR_UNSUPPORTED;
   }
@@ -380,9 +388,9 @@ extern "C" int ic_decode_step(const ic_step_args* a, void* stream) {
   ic_decode_args d = a->layer0;
   const int esz = dtype_size(d.pool.dtype);
   const int osz = dtype_size(d.out_dtype);
+  d.inputs_ready = 1;
   for (int l = 0; l < d.pool.num_layers; ++l) {
     d.layer = l;
-    d.accumulate = l > 0 ? 1 : 0;
     d.q = static_cast<const char*>(a->layer0.q) + static_cast<int64_t>(l) * a->q_layer_stride * esz;
     d.k_new = static_cast<const char*>(a->layer0.k_new) + static_cast<int64_t>(l) * a->kv_layer_stride * esz;
     d.v_new = static_cast<const char*>(a->layer0.v_new) + static_cast<int64_t>(l) * a->kv_layer_stride * esz;

@@ -9,5 +9,7 @@ namespace ic {
 
 // Tensor-core kernel A, one cluster per (session, KV head) (fp16 / bf16).
 int launch_decode_mma(const ic_decode_args& a, cudaStream_t stream);
+// Tensor-core kernel A, one CTA streams a whole (session, KV head) group.
+int launch_decode_stream(const ic_decode_args& a, cudaStream_t stream);
 
 }  // namespace ic

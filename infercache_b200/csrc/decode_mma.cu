@@ -95,7 +95,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
   // With programmatic dependent launch, layers after the first gather their
   // K/V rows before waiting on the previous kernel (only the eviction kernel
   // rewrites the slot table, and it completed before layer 0 let its
-  // dependents launch); q, the new K/V and the mass row come after the wait.
+  // dependents launch); q and the new K/V come after the wait unless the
+  // caller marked them ready for the whole step.
   const bool early = a.pdl && a.layer > 0;
   if (a.pdl && !early) grid_dependency_wait();
 
@@ -106,18 +107,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
   const int32_t* st = a.sess.slot_table + static_cast<size_t>(s) * ntot;
   const uint8_t* occ_g = a.sess.occupied + static_cast<size_t>(s) * budget;
 
-  // q A-fragments (rows g, and g + 8 when GP == 16) and the chunk's mass row
-  // accumulated over the step's earlier layers: loaded before the K/V traffic
-  // when possible so they do not queue behind it
-  float* mrow = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + t0;
-  float mprev[MAXT];
+  // q A-fragments (rows g, and g + 8 when GP == 16): loaded before the K/V
+  // traffic when possible so they do not queue behind it
   uint32_t qa[8][4];
   auto load_inputs = [&]() {
-#pragma unroll
-    for (int i = 0; i < MAXT; ++i) {
-      const int t = tid + i * MMA_THREADS;
-      mprev[i] = (a.accumulate && t < n) ? mrow[t] : 0.f;
-    }
     const T* qb = static_cast<const T*>(a.q) + (static_cast<size_t>(s) * Hq + static_cast<size_t>(h) * G) * MMA_D;
     const uint32_t* q0 = reinterpret_cast<const uint32_t*>(qb + static_cast<size_t>(g) * MMA_D);
     const uint32_t* q1 = reinterpret_cast<const uint32_t*>(qb + static_cast<size_t>(g + 8) * MMA_D);
@@ -130,7 +123,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
       qa[kk][3] = (GP > 8 && g + 8 < G) ? q1[w + 4] : 0u;
     }
   };
-  if (!early) load_inputs();
+  if (!early || a.inputs_ready) load_inputs();
 
   // -- 1. gather the chunk's rows ------------------------------------------------
   for (int t = tid; t < n; t += MMA_THREADS) {
@@ -162,7 +155,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
   }
   if (early) {
     grid_dependency_wait();
-    load_inputs();
+    if (!a.inputs_ready) load_inputs();
   }
   if (a.pdl) grid_launch_dependents();
   for (int i = tid; i < (npad - n) * VPR; i += MMA_THREADS) {
@@ -277,13 +270,13 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
   __syncthreads();
 
   // -- 4. received mass per slot, summed over the group's heads in order -------
-#pragma unroll
-  for (int i = 0; i < MAXT; ++i) {
-    const int t = tid + i * MMA_THREADS;
-    if (t < n) {
+  {
+    const size_t ML = static_cast<size_t>(a.mass_layers);
+    float* mrow = a.mass + ((static_cast<size_t>(s) * Hkv + h) * ntot + t0) * ML + a.layer;
+    for (int t = tid; t < n; t += MMA_THREADS) {
       float m = 0.f;
       for (int gg = 0; gg < G; ++gg) m += sc[gg * cp + t];
-      mrow[t] = a.accumulate ? mprev[i] + m : m;
+      mrow[static_cast<size_t>(t) * ML] = m;
     }
   }
 

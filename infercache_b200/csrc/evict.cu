@@ -46,14 +46,54 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   // 1. decay + boost of every occupied slot
   const float decay = a.decay;
   const float div = a.mass_div;
+  const int MH = a.mass_heads, ML = a.mass_layers;
   for (int j = tid; j < B; j += EV_THREADS) {
     float v = imp[j];
     if (occ[j]) {
       float add = 0.f;
       if (a.mass) {
-        const float* m = a.mass + static_cast<size_t>(s) * a.mass_rows * ntot + j;
-        float tot = m[0];
-        for (int r = 1; r < a.mass_rows; ++r) tot = __fadd_rn(tot, m[static_cast<size_t>(r) * ntot]);
+        // The slot's mass is MH contiguous columns of ML layers.  Sum each
+        // column in layer order, then the columns in head order; all loads of
+        // a batch are issued before its adds.
+        const float* base = a.mass + (static_cast<size_t>(s) * MH * ntot + j) * ML;
+        const size_t hstride = static_cast<size_t>(ntot) * ML;
+        float tot = 0.f, acc = 0.f;
+        if ((ML & 3) == 0) {
+          constexpr int NV = 20;  // float4 loads per batch
+          const int per_h = ML / 4, nvec = MH * per_h;
+          for (int v0 = 0; v0 < nvec; v0 += NV) {
+            float4 x[NV];
+#pragma unroll
+            for (int u = 0; u < NV; ++u) {
+              const int vi = v0 + u;
+              x[u] = vi < nvec ? *reinterpret_cast<const float4*>(base + (vi / per_h) * hstride + (vi % per_h) * 4)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < NV; ++u) {
+              const int vi = v0 + u;
+              if (vi >= nvec) break;
+              const int hh = vi / per_h, l4 = vi % per_h;
+              const float xs[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) acc = (l4 == 0 && q == 0) ? xs[q] : __fadd_rn(acc, xs[q]);
+              if (l4 == per_h - 1) tot = hh == 0 ? acc : __fadd_rn(tot, acc);
+            }
+          }
+        } else {
+          for (int hh = 0; hh < MH; ++hh) {
+            const float* m = base + hh * hstride;
+            for (int l0 = 0; l0 < ML; l0 += 8) {
+              float x[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) x[u] = l0 + u < ML ? m[l0 + u] : 0.f;
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                if (l0 + u < ML) acc = (l0 + u == 0) ? x[u] : __fadd_rn(acc, x[u]);
+            }
+            tot = hh == 0 ? acc : __fadd_rn(tot, acc);
+          }
+        }
         add = __fdiv_rn(tot, div);
       }
       v = __fadd_rn(__fmul_rn(v, decay), add);
@@ -280,7 +320,7 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
   if (a->sess.num_sessions == 0) return IC_OK;
   if (!tiers_ok(a->tiers) || a->sess.num_sessions < 0 || !a->new_pos || !a->sess.slot_table ||
       !a->sess.positions || !a->sess.importance || !a->sess.occupied || !a->sess.ctrl ||
-      !a->sess.counters || (a->mass && (a->mass_rows < 1 || !(a->mass_div > 0.f)))) {
+      !a->sess.counters || (a->mass && (a->mass_heads < 1 || a->mass_layers < 1 || !(a->mass_div > 0.f)))) {
     set_last_error("evict_update: bad arguments");
     return IC_ERR_INVALID_ARG;
   }

@@ -141,7 +141,8 @@ class SessionBatch:
         self.ctrl[:, _lib.IC_CTRL_RECENT_PTR] = cfg.recent_start
         self.counters = torch.zeros((S, _lib.IC_COUNTER_WORDS), dtype=torch.int64, device=dev)
         self.dev_status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.mass = torch.zeros((S, cfg.num_kv_heads, ntot), dtype=torch.float32, device=dev)
+        # received mass of each slot per KV head and layer (layer innermost)
+        self.mass = torch.zeros((S, cfg.num_kv_heads, ntot, cfg.num_layers), dtype=torch.float32, device=dev)
         self.events = torch.full((S, 4), -1, dtype=torch.int64, device=dev)
         self._pos_buf = torch.zeros(S, dtype=torch.int64, device=dev)
         self.scale = cfg.head_dim ** -0.5
@@ -155,9 +156,10 @@ class SessionBatch:
                                         counters=self.counters.data_ptr(), dev_status=self.dev_status.data_ptr())
         self._c_pool = pool.c_pool()
         self._dec = _lib.ic_decode_args(pool=self._c_pool, tiers=self._c_tiers, sess=self._c_sess,
-                                        mass=self.mass.data_ptr(), scale=self.scale)
+                                        mass=self.mass.data_ptr(), scale=self.scale, mass_layers=cfg.num_layers)
         self._ev = _lib.ic_evict_args(tiers=self._c_tiers, sess=self._c_sess, mass=self.mass.data_ptr(),
-                                      mass_rows=cfg.num_kv_heads, mass_div=float(cfg.num_layers * cfg.num_kv_heads),
+                                      mass_heads=cfg.num_kv_heads, mass_layers=cfg.num_layers,
+                                      mass_div=float(cfg.num_layers * cfg.num_kv_heads),
                                       decay=cfg.decay, new_pos=self._pos_buf.data_ptr(),
                                       events=self.events.data_ptr())
         # programmatic dependent launch between the step's kernels
@@ -193,7 +195,7 @@ class SessionBatch:
         d.v_new = v.data_ptr()
         d.out = out.data_ptr()
         d.out_dtype = _lib.dtype_code(out.dtype)
-        d.accumulate = 1 if layer > 0 else 0
+        d.inputs_ready = 0
         _lib.call("ic_decode_layer", d)
         return out
 
@@ -212,7 +214,8 @@ class SessionBatch:
         e.new_pos = pos.data_ptr()
         e.decay = self.cfg.decay if decay is None else float(decay)
         e.mass = self.mass.data_ptr()
-        e.mass_rows = self.cfg.num_kv_heads
+        e.mass_heads = self.cfg.num_kv_heads
+        e.mass_layers = self.cfg.num_layers
         e.mass_div = float(self.cfg.num_layers * self.cfg.num_kv_heads)
         e.pdl = 1 if self.pdl else 0
         _lib.call("ic_evict_update", e)
@@ -286,13 +289,14 @@ class SessionBatch:
             w = w.contiguous()
             Lw, Hw, Qw, F = w.shape
             srt, fill = self._sort(sub)
-            mass = torch.empty((1, 1, cfg.total_budget + 1), dtype=torch.float32, device=self.device)
+            mass = torch.empty((1, cfg.total_budget + 1), dtype=torch.float32, device=self.device)
             b = _lib.ic_boost_args(tiers=self._c_tiers, num_sessions=1, L=Lw, H=Hw, Q=Qw, width=F,
                                    weights=w.data_ptr(), sorted_slots=srt.data_ptr(), fill=fill.data_ptr(),
                                    mass_out=mass.data_ptr())
             _lib.call("ic_boost_sorted", b)
         pos = torch.tensor([int(position)], dtype=torch.int64).to(self.device, non_blocking=True)
-        e = _lib.ic_evict_args(tiers=self._c_tiers, sess=sub, mass=_lib.ptr(mass), mass_rows=1, mass_div=1.0,
+        e = _lib.ic_evict_args(tiers=self._c_tiers, sess=sub, mass=_lib.ptr(mass), mass_heads=1, mass_layers=1,
+                               mass_div=1.0,
                                decay=1.0, new_pos=pos.data_ptr(),
                                events=self.events[session:].data_ptr())
         _lib.call("ic_evict_update", e)

@@ -52,9 +52,11 @@ def test_small_protocol(golden, name):
 
 
 @pytest.mark.parametrize("name", ["f16", "g7"])
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 def test_small_protocol_variants(name, variant):
-    """Both kernel-A implementations (CUDA cores, tensor cores) against the oracle."""
+    """Every kernel-A implementation (CUDA cores; tensor cores with one
+    cluster per group; tensor cores streaming a group per CTA) against the
+    oracle."""
     cache, oc, outs, events = run_small(name, variant=variant)
     cache.batch.check_device_status()
 
@@ -154,7 +156,8 @@ def test_batch_sessions_vs_oracle():
     b.check_device_status()
 
 
-def test_config2_full_size():
+@pytest.mark.parametrize("variant", [2, 3])
+def test_config2_full_size(variant):
     """The bench workload at full size: 36 layers, 16 sessions, 16/2 heads,
     budget 4/256/780, fp16, 2048-token prompts.  Session 0 is checked against
     the oracle step by step; all sessions are checked for invariants; a second
@@ -168,6 +171,7 @@ def test_config2_full_size():
 
     def build():
         b = SessionBatch(cfg, S, "cuda:0")
+        b.kernel_variant = variant
         for s in range(S):
             b.load_prompt(s, tuple((prompts[s][0][l][None].cuda(), prompts[s][1][l][None].cuda())
                                    for l in range(L)), prompts[s][2])
@@ -292,7 +296,6 @@ def test_evict_kernel_ties_exact():
     b.ctrl[:, _lib.IC_CTRL_IMPORTANT_FILL] = 6
     b.ctrl[:, _lib.IC_CTRL_RECENT_PTR] = 2
     b.mass.zero_()
-    b.mass[1, :, 2] = 0.0
     rows0 = b.slot_table.clone()
     b.evict([500, 501], decay=1.0)
     ev = b.events.cpu().tolist()
@@ -306,12 +309,14 @@ def test_evict_kernel_ties_exact():
     assert b.positions[0, 2].item() == 500 and b.positions[0, 7].item() == 102
     # decay + mass arithmetic on one session, rounded step by step
     g = torch.Generator().manual_seed(2)
-    m = torch.rand(2, 2, B + 1, generator=g)
+    m = torch.rand(2, 2, B + 1, 3, generator=g)  # [S, Hkv, slot, layer]
     b.mass.copy_(m)
     before = b.importance.clone()
     b.evict([600, 601], decay=0.75)
+    mn = m.numpy()
+    heads = [((mn[:, hh, :B, 0] + mn[:, hh, :B, 1]) + mn[:, hh, :B, 2]).astype(np.float32) for hh in range(2)]
     want = (before.cpu().numpy() * np.float32(0.75)).astype(np.float32) + \
-           ((m[:, 0, :B].numpy() + m[:, 1, :B].numpy()) / np.float32(6.0)).astype(np.float32)
+           ((heads[0] + heads[1]) / np.float32(6.0)).astype(np.float32)
     got = b.importance.cpu().numpy()
     ev2 = b.events.cpu().numpy()
     mask = np.ones_like(got, bool)
