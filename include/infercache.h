@@ -339,20 +339,32 @@ typedef struct ic_page_rows_args {
 int ic_page_gather(const ic_page_rows_args* a, void* stream);
 int ic_page_write(const ic_page_rows_args* a, void* stream);
 
-/* ---- Kernel C: summary-pass scorer (tcgen05 / TMEM, bf16) -----------------
- * Causal GQA attention over a prompt: O = softmax(scale * Q K^T) V with the
- * row log-sum-exp, and colsum[b, j] = sum_h sum_i P[b, h, i, j], the column
- * sums _attention_mass takes (two_pass.py:104-137), without materialising P.
- * q: [B, Hq, T, D]; k, v: [B, Hkv, T, D]; out [B, Hq, T, D] (may be NULL);
- * lse float [B, Hq, T]; colsum float [B, T].  bf16, D = 128, T % 128 == 0. */
+/* ---- Kernel C: summary-pass scorer (tcgen05 / TMEM) -----------------------
+ * Causal GQA attention over a prompt, P = softmax(scale * Q K^T) with query
+ * head h reading KV head h / (Hq / Hkv):
+ *   out[b, h, i, :]    = sum_j P[b, h, i, j] V[b, h / G, j, :]   (if out != NULL)
+ *   lse[b, h, i]       = natural-log log-sum-exp of row i
+ *   head_mass[b, h, j] = sum_i P[b, h, i, j]
+ *   colsum[b, j]       = sum_h head_mass[b, h, j]  (+= when accumulate != 0,
+ *                        summing layers as all_layers does)
+ *   importance[b, j]   = colsum[b, j] / sum_j colsum[b, j] when that total
+ *                        exceeds 1e-9, else colsum (if importance != NULL)
+ * the received attention mass of _attention_mass (two_pass.py:104-137),
+ * computed without materialising P.  q [B, Hq, T, D], k / v [B, Hkv, T, D]
+ * contiguous, fp16 or bf16 (dtype), D = 128, any T >= 1; base pointers
+ * 16-byte aligned.  Float outputs are caller-allocated. */
 typedef struct ic_summary_args {
   const void* q;
   const void* k;
-  const void* v;
-  void* out;
-  float* lse;
-  float* colsum;
+  const void* v;            /* may be NULL when out is NULL */
+  void* out;                /* [B, Hq, T, D] (q's dtype) or NULL */
+  float* lse;               /* [B, Hq, T] */
+  float* head_mass;         /* [B, Hq, T] */
+  float* colsum;            /* [B, T] */
+  float* importance;        /* [B, T] or NULL */
   int32_t batch, num_q_heads, num_kv_heads, seq_len, head_dim;
+  int32_t dtype;            /* IC_F16 or IC_BF16 */
+  int32_t accumulate;
   float scale;
   int32_t* dev_status;
 } ic_summary_args;

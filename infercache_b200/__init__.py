@@ -6,6 +6,7 @@ Public API (the reference's names):
     SessionBatch                                       batched sessions + hot-path verbs
     PAGE_SIZE, PagedCacheConfig, PagePool, KVAllocator,
     PagedSessionView, MultiSessionCache                paged_cache
+    summary_score, attention_mass, SummaryScores       summary (kernel C)
     TwoPassConfig, SummaryResult, TwoPassEngine        two_pass
     gather_cache_kv, scatter_importance, topk_min_slot,
     compact_sdp_attention, GPUImportanceTracker        cache_ops (the triton_ops names)
@@ -15,5 +16,6 @@ Importing the package needs no GPU; constructing a cache does.
 from .hierarchical_cache import CacheConfig, CacheStats, HierarchicalKVCache, SessionBatch  # noqa: F401
 from .paged_cache import (PAGE_SIZE, KVAllocator, MultiSessionCache, PagedCacheConfig,  # noqa: F401
                           PagedSessionView, PagePool)
+from .summary import SummaryScores, attention_mass, summary_score  # noqa: F401
 
 __version__ = "0.1.0"

@@ -140,8 +140,9 @@ class ic_page_rows_args(Structure):
 
 class ic_summary_args(Structure):
     _fields_ = [("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("out", c_void_p), ("lse", c_void_p),
-                ("colsum", c_void_p), ("batch", c_int32), ("num_q_heads", c_int32),
-                ("num_kv_heads", c_int32), ("seq_len", c_int32), ("head_dim", c_int32), ("scale", c_float),
+                ("head_mass", c_void_p), ("colsum", c_void_p), ("importance", c_void_p),
+                ("batch", c_int32), ("num_q_heads", c_int32), ("num_kv_heads", c_int32), ("seq_len", c_int32),
+                ("head_dim", c_int32), ("dtype", c_int32), ("accumulate", c_int32), ("scale", c_float),
                 ("dev_status", c_void_p)]
 
 

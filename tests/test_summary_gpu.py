@@ -1,0 +1,171 @@
+"""Kernel C (summary-pass scorer) against the oracle and the reference's
+attention mass, on a B200.
+
+Tolerances (written here, used below):
+* received mass (head_mass, colsum) and importance: elementwise relative
+  1e-3 (the fp16 / bf16 bar) — the kernel sums exact fp32 exponentials, so
+  the observed error is ~1e-5.
+* row log-sum-exp: absolute 1e-3 (natural log units, values ~ log T).
+* attention output O: normwise per row, 4e-3 for fp16 and 1.6e-2 for bf16 —
+  P enters the P.V product as a 16-bit value (relative rounding 2^-11 /
+  2^-8) and O is stored in the input dtype; the fp32 reference is exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+import specs
+from oracle.summary import attention_mass, tier_fill
+from tolerances import elem_close, rows_err
+
+pytestmark = pytest.mark.gpu
+
+O_TOL = {torch.float16: 4e-3, torch.bfloat16: 1.6e-2}
+
+
+def ref_attention(q, k, v, scale):
+    """fp32 causal GQA attention on the GPU: O, lse, per-head received mass."""
+    B, Hq, T, D = q.shape
+    G = Hq // k.shape[1]
+    kf = k.float().repeat_interleave(G, dim=1)
+    vf = v.float().repeat_interleave(G, dim=1) if v is not None else None
+    s = torch.matmul(q.float(), kf.transpose(-1, -2)) * scale
+    mask = torch.ones(T, T, dtype=torch.bool, device=q.device).tril()
+    s = s.masked_fill(~mask, float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    p = torch.exp(s - lse[..., None])
+    o = torch.matmul(p, vf) if vf is not None else None
+    return o, lse, p.sum(dim=2)
+
+
+def rand_qkv(B, Hq, Hkv, T, dtype, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(B, Hq, T, 128, generator=g, device="cuda").to(dtype)
+    k = torch.randn(B, Hkv, T, 128, generator=g, device="cuda").to(dtype)
+    v = torch.randn(B, Hkv, T, 128, generator=g, device="cuda").to(dtype)
+    return q, k, v
+
+
+SHAPES = [(1, 2, 1, 128), (2, 4, 2, 256), (1, 16, 2, 300), (1, 8, 8, 1), (1, 2, 1, 129), (2, 16, 2, 640)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_summary_vs_fp32_reference(shape, dtype):
+    from infercache_b200.summary import summary_score
+    B, Hq, Hkv, T = shape
+    q, k, v = rand_qkv(B, Hq, Hkv, T, dtype, seed=T * 7 + Hq)
+    scale = 128 ** -0.5
+    res = summary_score(q, k, v, scale=scale)
+    o_ref, lse_ref, hm_ref = ref_attention(q, k, v, scale)
+    torch.cuda.synchronize()
+    assert np.abs(res.lse.cpu().numpy() - lse_ref.cpu().numpy()).max() < 1e-3
+    err = rows_err(res.out.float().cpu().numpy().reshape(-1, 128), o_ref.cpu().numpy().reshape(-1, 128))
+    assert err < O_TOL[dtype], f"O normwise error {err}"
+    assert elem_close(res.head_mass.cpu().numpy(), hm_ref.cpu().numpy(), 1e-3)
+    cs_ref = hm_ref.sum(dim=1)
+    assert elem_close(res.colsum.cpu().numpy(), cs_ref.cpu().numpy(), 1e-3)
+    imp_ref = cs_ref / cs_ref.sum(dim=1, keepdim=True)
+    assert elem_close(res.importance.cpu().numpy(), imp_ref.cpu().numpy(), 1e-3)
+
+
+def test_summary_without_output_matches():
+    """out = NULL takes the statistics-only kernel; lse and mass must agree."""
+    from infercache_b200.summary import summary_score
+    q, k, v = rand_qkv(1, 16, 2, 512, torch.bfloat16, seed=5)
+    a = summary_score(q, k, v)
+    b = summary_score(q, k, None, with_output=False)
+    torch.cuda.synchronize()
+    assert b.out is None
+    assert np.abs(a.lse.cpu().numpy() - b.lse.cpu().numpy()).max() < 1e-5
+    assert elem_close(b.colsum.cpu().numpy(), a.colsum.cpu().numpy(), 1e-5)
+
+
+def test_summary_deterministic():
+    from infercache_b200.summary import summary_score
+    q, k, v = rand_qkv(2, 16, 2, 1024, torch.bfloat16, seed=9)
+    a = summary_score(q, k, v)
+    b = summary_score(q, k, v)
+    torch.cuda.synchronize()
+    assert torch.equal(a.colsum, b.colsum) and torch.equal(a.lse, b.lse) and torch.equal(a.out, b.out)
+
+
+def test_attention_mass_golden(golden):
+    """The reference's _attention_mass (fixture) and its tier fill, from q / k."""
+    from infercache_b200.summary import attention_mass as gpu_mass
+    g = golden("attn_mass")
+    sp = specs.AMASS
+    q, k, _ = specs.amass_inputs()
+    qd = q[None].to("cuda", torch.bfloat16)
+    kd = k[None].to("cuda", torch.bfloat16)
+    imp = gpu_mass([(qd, kd)]).cpu().numpy()
+    assert elem_close(imp, g["scores"], 1e-3)
+    # the oracle restatement agrees with the fixture too
+    _, imp_o = attention_mass(q.numpy(), k.numpy())
+    assert elem_close(imp_o, g["scores"], 1e-5)
+    # tier fill: exact on the GPU's own scores; vs the fixture only near-ties may differ
+    tf_gpu = tier_fill(imp, None, sp["sink"], sp["recent"], sp["important"])
+    sel_gpu = set(tf_gpu["slot_token"][tf_gpu["occupied"]].tolist())
+    sel_ref = set(g["slot_token"][g["occupied"]].tolist())
+    diff = sel_gpu ^ sel_ref
+    if diff:
+        T = g["scores"].shape[0]
+        l2_ref = [t for t in sel_ref if sp["sink"] <= t < T - sp["recent"]]
+        cut = float(np.min(g["scores"][l2_ref]))
+        for t in diff:
+            assert abs(float(g["scores"][t]) - cut) <= 1e-3 * cut, f"token {t} differs beyond a near-tie"
+
+
+def test_attention_mass_all_layers_accumulates():
+    from infercache_b200.summary import attention_mass as gpu_mass, summary_score
+    layers = [rand_qkv(1, 16, 2, 384, torch.bfloat16, seed=40 + i)[:2] for i in range(3)]
+    imp = gpu_mass(layers, all_layers=True)
+    tot = sum(summary_score(q, k, None, with_output=False).colsum for q, k in layers)
+    ref = tot / tot.sum()
+    assert elem_close(imp.cpu().numpy(), ref[0].cpu().numpy(), 1e-5)
+    one = gpu_mass(layers, all_layers=False, layer_idx=-1)
+    ref1 = summary_score(*layers[-1], None, with_output=False).importance[0]
+    assert torch.equal(one, ref1)
+
+
+def test_summary_full_size_properties():
+    """Config-4 size (8 sequences x 16 heads x 8192 tokens): every row of P sums
+    to 1, so each head's received mass totals T; sampled rows of O and lse
+    match an fp32 recomputation."""
+    from infercache_b200.summary import summary_score
+    B, Hq, Hkv, T = 8, 16, 2, 8192
+    q, k, v = rand_qkv(B, Hq, Hkv, T, torch.bfloat16, seed=3)
+    res = summary_score(q, k, v)
+    torch.cuda.synchronize()
+    st = res.head_mass.double().sum(dim=2)
+    assert torch.allclose(st, torch.full_like(st, T), rtol=1e-4)
+    assert torch.all(torch.isfinite(res.importance))
+    scale = 128 ** -0.5
+    for b, h, rows in [(0, 0, [0, 1, 127, 128, 4095, 8191]), (7, 15, [5, 1000, 8190]), (3, 9, [2048, 6000])]:
+        kf = k[b, h // 8].float()
+        for i in rows:
+            s = (q[b, h, i].float() @ kf[: i + 1].T) * scale
+            lse = torch.logsumexp(s, 0)
+            o = torch.softmax(s, 0) @ v[b, h // 8, : i + 1].float()
+            assert abs(float(res.lse[b, h, i]) - float(lse)) < 1e-3
+            e = float((res.out[b, h, i].float() - o).abs().max() / o.abs().max())
+            assert e < O_TOL[torch.bfloat16], (b, h, i, e)
+    # a sampled column of the received mass against its definition
+    j = 4000
+    s = torch.einsum("hid,d->hi", q[0, :, j:].float(), k[0, 0, j].float()) * scale  # heads 0..7 read KV head 0
+    p = torch.exp(s[:8] - res.lse[0, :8, j:])
+    assert abs(float(p.sum(dim=1)[0]) - float(res.head_mass[0, 0, j])) <= 1e-3 * float(res.head_mass[0, 0, j])
+
+
+def test_summary_rejects_bad_args():
+    from infercache_b200 import _lib
+    from infercache_b200.summary import summary_score
+    q, k, v = rand_qkv(1, 4, 2, 128, torch.bfloat16, seed=1)
+    with pytest.raises(ValueError):
+        summary_score(q.float(), k.float(), v.float())
+    with pytest.raises(ValueError):
+        summary_score(q[:, :3], k, v)
+    qq = torch.randn(1, 4, 128, 64, device="cuda", dtype=torch.bfloat16)
+    kk = torch.randn(1, 2, 128, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(_lib.Unsupported):
+        summary_score(qq, kk, None, with_output=False)
