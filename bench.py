@@ -181,6 +181,56 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+SUMMARY_WORKLOAD = dict(batch=8, hq=16, hkv=2, T=8192, d=128)
+
+
+def summary_leg(device, iters=10, batch=None):
+    """Kernel C on the summary-pass workload: 8 sequences x 16/2 heads x 8192
+    tokens, causal, bf16 (seeded synthetic q / k / v).  Algorithmic work is the
+    causal QK^T + PV: 4 * B * Hq * D * T (T + 1) / 2 flops; the column-sum
+    sweep's extra QK^T is overhead, not work."""
+    from infercache_b200.summary import summary_score
+    w = SUMMARY_WORKLOAD
+    B, Hq, Hkv, T, D = batch or w["batch"], w["hq"], w["hkv"], w["T"], w["d"]
+    g = torch.Generator(device=device).manual_seed(3)
+    q = torch.randn(B, Hq, T, D, generator=g, device=device).bfloat16()
+    k = torch.randn(B, Hkv, T, D, generator=g, device=device).bfloat16()
+    v = torch.randn(B, Hkv, T, D, generator=g, device=device).bfloat16()
+    st = torch.zeros(1, dtype=torch.int32, device=device)
+    run = lambda: summary_score(q, k, v, status=st, check_status=False)  # noqa: E731
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    if int(st.item()):
+        raise RuntimeError(f"summary_score device status {int(st.item()):#x}")
+    ms = e0.elapsed_time(e1) / iters
+    flops = 4 * B * Hq * D * T * (T + 1) / 2
+    peak, kind = measured_tensor_peak()
+    tflops = flops / (ms / 1e3) / 1e12
+    del q, k, v
+    return {"workload": f"summary pass: {B} sequences x {Hq}/{Hkv} heads x {T} tokens causal, head_dim {D}, bf16",
+            "kernels": "summary_fwd_kernel + summary_colsum_kernel + summary_reduce_kernel (ic_summary_score)",
+            "ms_per_call": ms, "alg_tflop_per_call": flops / 1e12,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "peak_kind": f"{kind} (MEASURED_PEAKS.json bf16_tflops, burst)"}}
+
+
 # ---- our arm ----------------------------------------------------------------------------------
 def build_batch(spec, device, seed):
     from infercache_b200 import CacheConfig, SessionBatch
@@ -209,6 +259,10 @@ def main():
     ap.add_argument("--cluster", type=int, default=0)
     ap.add_argument("--no-graph", action="store_true", help="replay steps eagerly instead of as a CUDA graph")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-summary", action="store_true", help="skip the summary-pass scorer leg")
+    ap.add_argument("--workload", choices=["decode", "summary"], default="decode",
+                    help="summary: time only the summary-pass scorer (for profiling)")
+    ap.add_argument("--summary-batch", type=int, default=0, help="sequences in the summary workload")
     args = ap.parse_args()
     faulthandler.enable()
     args.warmup = max(3, args.warmup)
@@ -221,6 +275,10 @@ def main():
     import torch.distributed as dist
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    if args.workload == "summary":
+        if rank == 0:
+            print(json.dumps(summary_leg(device, iters=args.steps, batch=args.summary_batch or None)), flush=True)
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
@@ -354,6 +412,11 @@ def main():
     d2h = out.numel() * out.element_size()
     b.check_device_status()
 
+    summ = None
+    if not args.no_summary:
+        log("summary leg")
+        summ = summary_leg(device)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(spec)
@@ -375,7 +438,8 @@ def main():
                         "steps": ke, "api": "SessionBatch.step (ic_decode_step) with pinned host buffers"},
                 "gpu_launches": args.steps * (L + 1),
                 "clocks": sampler.summary() if sampler else None,
-                "cuda_graph": not args.no_graph}
+                "cuda_graph": not args.no_graph,
+                "summary_score": summ}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphs
