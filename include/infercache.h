@@ -352,15 +352,17 @@ int ic_page_write(const ic_page_rows_args* a, void* stream);
  * the received attention mass of _attention_mass (two_pass.py:104-137),
  * computed without materialising P.  q [B, Hq, T, D], k / v [B, Hkv, T, D]
  * contiguous, fp16 or bf16 (dtype), D = 128, any T >= 1; base pointers
- * 16-byte aligned.  Float outputs are caller-allocated. */
+ * 16-byte aligned.  Float outputs are caller-allocated.  With head_mass NULL
+ * only out and lse are computed (a causal prefill attention; colsum and
+ * importance are then ignored). */
 typedef struct ic_summary_args {
   const void* q;
   const void* k;
   const void* v;            /* may be NULL when out is NULL */
   void* out;                /* [B, Hq, T, D] (q's dtype) or NULL */
   float* lse;               /* [B, Hq, T] */
-  float* head_mass;         /* [B, Hq, T] */
-  float* colsum;            /* [B, T] */
+  float* head_mass;         /* [B, Hq, T] or NULL */
+  float* colsum;            /* [B, T] (required with head_mass) */
   float* importance;        /* [B, T] or NULL */
   int32_t batch, num_q_heads, num_kv_heads, seq_len, head_dim;
   int32_t dtype;            /* IC_F16 or IC_BF16 */
@@ -369,6 +371,64 @@ typedef struct ic_summary_args {
   int32_t* dev_status;
 } ic_summary_args;
 int ic_summary_score(const ic_summary_args* a, void* stream);
+
+/* ---- tensor-level helpers with the triton_ops names ---------------------------
+ * For callers holding plain K / V buffers and an importance vector (the fused
+ * path does not use them). */
+
+/* gather_cache_kv (triton_ops.py:107-135): out[h, f, :] = src[h, idx[f], :]
+ * (zeros for an index outside [0, N)).  src strides in elements, rows
+ * contiguous; rows and bases 16-byte aligned. */
+typedef struct ic_index_rows_args {
+  const void* src;
+  void* out;                /* [H, F, D] contiguous */
+  const int64_t* idx;       /* [F] */
+  int64_t stride_h, stride_n;
+  int32_t H, N, F, D;
+  int32_t dtype;
+  int32_t _pad;
+} ic_index_rows_args;
+int ic_index_rows(const ic_index_rows_args* a, void* stream);
+
+/* scatter_importance (triton_ops.py:148-175): for f < min(width, n_slots),
+ * importance[slots[f]] += (sum over the `rows` rows of weights[r, f]) / rows,
+ * weights float [rows, width] (rows = L * H * Q). */
+typedef struct ic_scatter_mass_args {
+  const float* weights;
+  const int64_t* slots;
+  float* importance;        /* [budget] */
+  int32_t rows, width, n_slots, budget;
+} ic_scatter_mass_args;
+int ic_scatter_mass(const ic_scatter_mass_args* a, void* stream);
+
+/* topk_min_slot (triton_ops.py:207-235): *out_idx = start + first index of the
+ * minimum of x[start, start + n) (NaN counts as smallest); *out_val its
+ * value (out_val may be NULL). */
+typedef struct ic_argmin_args {
+  const float* x;
+  int32_t start, n;
+  int64_t* out_idx;
+  float* out_val;
+} ic_argmin_args;
+int ic_argmin_range(const ic_argmin_args* a, void* stream);
+
+/* compact_sdp_attention (triton_ops.py:251-287): out[b, h, :] =
+ * softmax(scale * q[b, h, :] . K[h, slots[f], :]) V[h, slots[f], :] over f.
+ * q / out [B, H, D] contiguous; K / V buffers [H, budget, D] with the given
+ * element strides; D a multiple of 32 up to 256. */
+typedef struct ic_compact_attn_args {
+  const void* q;
+  const void* k_buf;
+  const void* v_buf;
+  const int64_t* slots;     /* [F] */
+  void* out;
+  int64_t k_stride_h, k_stride_n, v_stride_h, v_stride_n;
+  int32_t B, H, F, D, budget;
+  int32_t dtype;
+  float scale;
+  int32_t _pad;
+} ic_compact_attn_args;
+int ic_compact_attention(const ic_compact_attn_args* a, void* stream);
 
 /* ---- library information --------------------------------------------------*/
 const char* ic_status_str(int status);

@@ -17,5 +17,8 @@ from .hierarchical_cache import CacheConfig, CacheStats, HierarchicalKVCache, Se
 from .paged_cache import (PAGE_SIZE, KVAllocator, MultiSessionCache, PagedCacheConfig,  # noqa: F401
                           PagedSessionView, PagePool)
 from .summary import SummaryScores, attention_mass, summary_score  # noqa: F401
+from .two_pass import SummaryResult, TwoPassConfig, TwoPassEngine  # noqa: F401
+from .cache_ops import (GPUImportanceTracker, compact_sdp_attention, gather_cache_kv,  # noqa: F401
+                        scatter_importance, topk_min_slot)
 
 __version__ = "0.1.0"

@@ -146,6 +146,28 @@ class ic_summary_args(Structure):
                 ("dev_status", c_void_p)]
 
 
+class ic_index_rows_args(Structure):
+    _fields_ = [("src", c_void_p), ("out", c_void_p), ("idx", c_void_p), ("stride_h", c_int64),
+                ("stride_n", c_int64), ("H", c_int32), ("N", c_int32), ("F", c_int32), ("D", c_int32),
+                ("dtype", c_int32), ("_pad", c_int32)]
+
+
+class ic_scatter_mass_args(Structure):
+    _fields_ = [("weights", c_void_p), ("slots", c_void_p), ("importance", c_void_p), ("rows", c_int32),
+                ("width", c_int32), ("n_slots", c_int32), ("budget", c_int32)]
+
+
+class ic_argmin_args(Structure):
+    _fields_ = [("x", c_void_p), ("start", c_int32), ("n", c_int32), ("out_idx", c_void_p), ("out_val", c_void_p)]
+
+
+class ic_compact_attn_args(Structure):
+    _fields_ = [("q", c_void_p), ("k_buf", c_void_p), ("v_buf", c_void_p), ("slots", c_void_p), ("out", c_void_p),
+                ("k_stride_h", c_int64), ("k_stride_n", c_int64), ("v_stride_h", c_int64),
+                ("v_stride_n", c_int64), ("B", c_int32), ("H", c_int32), ("F", c_int32), ("D", c_int32),
+                ("budget", c_int32), ("dtype", c_int32), ("scale", c_float), ("_pad", c_int32)]
+
+
 # entry point name -> argument struct (None for the library-information calls)
 ENTRY_POINTS = {
     "ic_decode_layer": ic_decode_args,
@@ -161,6 +183,10 @@ ENTRY_POINTS = {
     "ic_page_gather": ic_page_rows_args,
     "ic_page_write": ic_page_rows_args,
     "ic_summary_score": ic_summary_args,
+    "ic_index_rows": ic_index_rows_args,
+    "ic_scatter_mass": ic_scatter_mass_args,
+    "ic_argmin_range": ic_argmin_args,
+    "ic_compact_attention": ic_compact_attn_args,
 }
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
 

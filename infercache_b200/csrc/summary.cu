@@ -601,6 +601,7 @@ int launch_summary(const ic_summary_args* a, cudaStream_t st) {
     summary_fwd_kernel<T, false><<<grid, FWD_THREADS, F_BYTES, st>>>(mq, mk, mv, p);
   }
   if ((rc = launch_status("summary_fwd_kernel")) != IC_OK) return rc;
+  if (!a->head_mass) return IC_OK;
   if ((rc = ensure_dynamic_smem(summary_colsum_kernel<T>, C_BYTES, &lim_col)) != IC_OK) return rc;
   summary_colsum_kernel<T><<<grid, COL_THREADS, C_BYTES, st>>>(mq, mk, p);
   if ((rc = launch_status("summary_colsum_kernel")) != IC_OK) return rc;
@@ -615,7 +616,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 }  // namespace ic
 
 extern "C" int ic_summary_score(const ic_summary_args* a, void* stream) {
-  if (!a || !a->q || !a->k || !a->lse || !a->head_mass || !a->colsum || !a->dev_status) {
+  if (!a || !a->q || !a->k || !a->lse || !a->dev_status || (a->head_mass && !a->colsum) ||
+      (!a->head_mass && !a->out)) {
     ic::set_last_error("summary_score: null argument");
     return IC_ERR_INVALID_ARG;
   }

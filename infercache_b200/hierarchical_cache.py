@@ -206,14 +206,16 @@ class SessionBatch:
         d.kernel_variant = self.kernel_variant
         d.pdl = 1 if self.pdl else 0
 
-    def evict(self, positions, decay: Optional[float] = None) -> None:
+    def evict(self, positions, decay: Optional[float] = None, use_mass: bool = True) -> None:
         """Kernel B once per step after the last layer.  positions: [S] int64
-        (tensor on this device, or a sequence of ints) of the decoded tokens."""
+        (tensor on this device, or a sequence of ints) of the decoded tokens.
+        ``use_mass=False`` skips the importance boost (a push without attention
+        weights, hierarchical_cache.py:259-261)."""
         pos = self._positions_arg(positions)
         e = self._ev
         e.new_pos = pos.data_ptr()
         e.decay = self.cfg.decay if decay is None else float(decay)
-        e.mass = self.mass.data_ptr()
+        e.mass = self.mass.data_ptr() if use_mass else 0
         e.mass_heads = self.cfg.num_kv_heads
         e.mass_layers = self.cfg.num_layers
         e.mass_div = float(self.cfg.num_layers * self.cfg.num_kv_heads)

@@ -22,8 +22,8 @@ from . import _lib
 class SummaryScores:
     out: Optional[torch.Tensor]   # [B, Hq, T, D] or None
     lse: torch.Tensor             # [B, Hq, T] float32, natural log
-    head_mass: torch.Tensor       # [B, Hq, T] float32
-    colsum: torch.Tensor          # [B, T] float32
+    head_mass: Optional[torch.Tensor]   # [B, Hq, T] float32
+    colsum: Optional[torch.Tensor]      # [B, T] float32
     importance: Optional[torch.Tensor]  # [B, T] float32, colsum / total
 
 
@@ -50,7 +50,7 @@ def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: Optional[torch.Tensor]):
 def summary_score(q: torch.Tensor, k: torch.Tensor, v: Optional[torch.Tensor] = None, *,
                   scale: Optional[float] = None, with_output: bool = True,
                   colsum: Optional[torch.Tensor] = None, accumulate: bool = False,
-                  normalise: bool = True, status: Optional[torch.Tensor] = None,
+                  normalise: bool = True, with_mass: bool = True, status: Optional[torch.Tensor] = None,
                   check_status: bool = True) -> SummaryScores:
     """One layer of the summary pass.
 
@@ -58,7 +58,9 @@ def summary_score(q: torch.Tensor, k: torch.Tensor, v: Optional[torch.Tensor] = 
     attention output (when ``with_output`` and v is given), the row
     log-sum-exp, per-head and head-summed received mass, and the normalised
     importance.  With ``accumulate`` the head-summed mass is added to
-    ``colsum`` (all layers of ``_attention_mass``).  ``check_status`` reads
+    ``colsum`` (all layers of ``_attention_mass``).  ``with_mass=False``
+    computes only the output and log-sum-exp (a causal prefill attention; the
+    mass fields are then None).  ``check_status`` reads
     the device status word after the launch (a synchronisation) and raises if
     a device-side wait timed out; pass False and a ``status`` tensor to keep
     the call asynchronous and check it later.
@@ -68,11 +70,15 @@ def summary_score(q: torch.Tensor, k: torch.Tensor, v: Optional[torch.Tensor] = 
     _lib.require_device(dev)
     q, k = q.contiguous(), k.contiguous()
     want_out = with_output and v is not None
+    if not with_mass and not want_out:
+        raise ValueError("nothing to compute: with_mass=False needs v and with_output")
     v = v.contiguous() if v is not None else None
     out = torch.empty_like(q) if want_out else None
     lse = torch.empty(B, Hq, T, dtype=torch.float32, device=dev)
-    head_mass = torch.empty(B, Hq, T, dtype=torch.float32, device=dev)
-    if colsum is None:
+    head_mass = torch.empty(B, Hq, T, dtype=torch.float32, device=dev) if with_mass else None
+    if not with_mass:
+        colsum, normalise = None, False
+    elif colsum is None:
         if accumulate:
             raise ValueError("accumulate needs the colsum to add to")
         colsum = torch.empty(B, T, dtype=torch.float32, device=dev)
@@ -83,7 +89,7 @@ def summary_score(q: torch.Tensor, k: torch.Tensor, v: Optional[torch.Tensor] = 
         status = torch.zeros(1, dtype=torch.int32, device=dev)
     a = _lib.ic_summary_args(
         q=q.data_ptr(), k=k.data_ptr(), v=_lib.ptr(v), out=_lib.ptr(out), lse=lse.data_ptr(),
-        head_mass=head_mass.data_ptr(), colsum=colsum.data_ptr(), importance=_lib.ptr(importance),
+        head_mass=_lib.ptr(head_mass), colsum=_lib.ptr(colsum), importance=_lib.ptr(importance),
         batch=B, num_q_heads=Hq, num_kv_heads=Hkv, seq_len=T, head_dim=D, dtype=_lib.dtype_code(q.dtype),
         accumulate=1 if accumulate else 0, scale=float(D ** -0.5 if scale is None else scale),
         dev_status=status.data_ptr())
