@@ -231,6 +231,65 @@ def summary_leg(device, iters=10, batch=None):
                          "frac": tflops / peak, "peak_kind": f"{kind} (MEASURED_PEAKS.json bf16_tflops, burst)"}}
 
 
+PAGED_WORKLOAD = dict(sessions=16, min_len=256, max_len=32768, layers=36, heads=2, d=128, seed=4)
+
+
+def paged_leg(device, iters=5):
+    """PagedSessionView gathers (kernel ic_page_gather) over whole sessions:
+    16 sessions with lengths U[256, 32768] (seed 4) in a 16-token page pool
+    of a 36-layer, 2-head, head_dim-128 fp16 model, pages handed out by the
+    reference's LIFO allocator.  Algorithmic bytes: every token's K and V of
+    every layer read once and written once to a contiguous [L, H, n, D]."""
+    from infercache_b200 import _lib
+    from infercache_b200.paged_cache import PAGE_SIZE, KVAllocator, PagedCacheConfig, PagePool
+    w = PAGED_WORKLOAD
+    g = torch.Generator().manual_seed(w["seed"])
+    lens = torch.randint(w["min_len"], w["max_len"] + 1, (w["sessions"],), generator=g).tolist()
+    pages = [-(-n // PAGE_SIZE) for n in lens]
+    n_pages = sum(pages)
+    L, H, D = w["layers"], w["heads"], w["d"]
+    pool = PagePool(PagedCacheConfig(n_pages=n_pages, n_layers=L, n_heads=H, head_dim=D, dtype=torch.float16,
+                                     device=str(device), max_pages_per_session=max(pages)))
+    alloc = KVAllocator(n_pages, max(pages))
+    plists = [[alloc.allocate_page(f"s{i}") for _ in range(p)] for i, p in enumerate(pages)]
+    gd = torch.Generator(device=device).manual_seed(w["seed"])
+    pool.K.normal_(generator=gd)
+    pool.V.normal_(generator=gd)
+    ok = torch.empty(L, H, max(lens), D, dtype=torch.float16, device=device)
+    ov = torch.empty_like(ok)
+    pids = [torch.tensor(pl, dtype=torch.int32, device=device) for pl in plists]
+    args = [_lib.ic_page_rows_args(pool=pool.c_pool(), page_ids=pid.data_ptr(), n_page_ids=len(pl), layer_begin=0,
+                                   layer_end=L, start_token=0, n_tokens=n, k_buf=ok.data_ptr(), v_buf=ov.data_ptr(),
+                                   stride_l=H * n * D, stride_h=n * D, stride_t=D)
+            for pid, pl, n in zip(pids, plists, lens)]
+
+    def run():
+        for a in args:
+            _lib.call("ic_page_gather", a)
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    tokens = sum(lens)
+    alg = tokens * L * H * D * 2 * 2 * 2  # K + V, fp16, read + write
+    peak, kind = measured_peak()
+    gbs = alg / (ms / 1e3) / 1e9
+    frag = (n_pages * PAGE_SIZE - tokens) / (n_pages * PAGE_SIZE)
+    del pool, ok, ov
+    return {"workload": f"paged gather: {w['sessions']} sessions, lengths U[{w['min_len']}, {w['max_len']}] "
+                        f"(seed {w['seed']}), {tokens} tokens, {L} layers x {H} heads x {D}, fp16, page 16",
+            "kernel": "page_rows_kernel (ic_page_gather), one launch per session",
+            "ms_per_pass": ms, "alg_bytes_per_pass": alg, "fragmentation": frag,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
+
+
 # ---- our arm ----------------------------------------------------------------------------------
 def build_batch(spec, device, seed):
     from infercache_b200 import CacheConfig, SessionBatch
@@ -412,10 +471,12 @@ def main():
     d2h = out.numel() * out.element_size()
     b.check_device_status()
 
-    summ = None
+    summ = paged = None
     if not args.no_summary:
         log("summary leg")
         summ = summary_leg(device)
+        log("paged gather leg")
+        paged = paged_leg(device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -439,7 +500,8 @@ def main():
                 "gpu_launches": args.steps * (L + 1),
                 "clocks": sampler.summary() if sampler else None,
                 "cuda_graph": not args.no_graph,
-                "summary_score": summ}
+                "summary_score": summ,
+                "paged_gather": paged}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphs

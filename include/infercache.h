@@ -157,7 +157,8 @@ enum ic_decode_variant {
   IC_DECODE_AUTO = 0,
   IC_DECODE_CUDA_CORES = 1,      /* fp32 / fp16 / bf16, one cluster per group   */
   IC_DECODE_TENSOR_CORES = 2,    /* fp16 / bf16, one cluster per group          */
-  IC_DECODE_TENSOR_STREAM = 3    /* fp16 / bf16, one CTA streams a whole group  */
+  IC_DECODE_TENSOR_STREAM = 3,   /* fp16 / bf16, one CTA streams a whole group  */
+  IC_DECODE_TENSOR_LEAN = 4      /* fp16 / bf16, one CTA, four warp pipelines   */
 };
 int ic_decode_layer(const ic_decode_args* a, void* stream);
 

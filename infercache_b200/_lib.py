@@ -36,6 +36,7 @@ IC_COUNTER_WORDS = 4
 IC_EV_NONE, IC_EV_DROP, IC_EV_FILL, IC_EV_EVICT, IC_EV_REJECT = 0, 1, 2, 3, 4
 IC_DEVFLAG_TIMEOUT, IC_DEVFLAG_BAD_ROW = 1, 2
 IC_DECODE_AUTO, IC_DECODE_CUDA_CORES, IC_DECODE_TENSOR_CORES, IC_DECODE_TENSOR_STREAM = 0, 1, 2, 3
+IC_DECODE_TENSOR_LEAN = 4
 
 DTYPE_CODE = {torch.float32: IC_F32, torch.float16: IC_F16, torch.bfloat16: IC_BF16}
 

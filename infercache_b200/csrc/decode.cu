@@ -359,13 +359,18 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int variant = a->kernel_variant;
-  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_STREAM) {
+  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_LEAN) {
     set_last_error("decode: bad kernel_variant");
     return IC_ERR_INVALID_ARG;
   }
-  // AUTO on fp16 / bf16: the streaming kernel when the step's inputs are all
-  // ready (consecutive layers then overlap), the cluster kernel otherwise
-  // (lowest latency for one layer at a time).
+  // AUTO on fp16 / bf16: when the step's inputs are all ready (consecutive
+  // layers then overlap) the lean kernel (up to 16 query heads per KV head,
+  // else the streaming kernel); one layer at a time, the cluster kernel
+  // (lowest latency for a single launch).
+  const int G = a->num_q_heads / a->pool.num_kv_heads;
+  if (a->pool.dtype != IC_F32 &&
+      (variant == IC_DECODE_TENSOR_LEAN || (variant == IC_DECODE_AUTO && a->inputs_ready && a->pdl && G <= 16)))
+    return launch_decode_lean(*a, st);
   if (a->pool.dtype != IC_F32 &&
       (variant == IC_DECODE_TENSOR_STREAM || (variant == IC_DECODE_AUTO && a->inputs_ready && a->pdl)))
     return launch_decode_stream(*a, st);

@@ -11,5 +11,7 @@ namespace ic {
 int launch_decode_mma(const ic_decode_args& a, cudaStream_t stream);
 // Tensor-core kernel A, one CTA streams a whole (session, KV head) group.
 int launch_decode_stream(const ic_decode_args& a, cudaStream_t stream);
+// Tensor-core kernel A, one CTA per group with four independent warp pipelines.
+int launch_decode_lean(const ic_decode_args& a, cudaStream_t stream);
 
 }  // namespace ic

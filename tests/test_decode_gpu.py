@@ -52,7 +52,7 @@ def test_small_protocol(golden, name):
 
 
 @pytest.mark.parametrize("name", ["f16", "g7"])
-@pytest.mark.parametrize("variant", [1, 2, 3])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4])
 def test_small_protocol_variants(name, variant):
     """Every kernel-A implementation (CUDA cores; tensor cores with one
     cluster per group; tensor cores streaming a group per CTA) against the
@@ -156,7 +156,7 @@ def test_batch_sessions_vs_oracle():
     b.check_device_status()
 
 
-@pytest.mark.parametrize("variant", [2, 3])
+@pytest.mark.parametrize("variant", [2, 3, 4])
 def test_config2_full_size(variant):
     """The bench workload at full size: 36 layers, 16 sessions, 16/2 heads,
     budget 4/256/780, fp16, 2048-token prompts.  Session 0 is checked against
