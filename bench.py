@@ -442,33 +442,28 @@ def main():
     torch.cuda.synchronize()
     seq_launch_s = max_over_ranks(d0.elapsed_time(d1)) / 1e3 / (kd * L)
 
-    # end to end through the public API: pinned host inputs -> device -> step -> host outputs
+    # end to end through the public API: each step copies q / k / v from pinned
+    # host buffers, runs the step and copies o back (SessionBatch.host_stepper,
+    # one CUDA graph per step)
     log("e2e")
     qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
     oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    qd, kd_, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    stepper = b.host_stepper(qh, kh, vh, oh, pos)
     ke = max(10, min(args.steps, 500))
     for _ in range(3):
-        qd.copy_(qh, non_blocking=True); kd_.copy_(kh, non_blocking=True); vd.copy_(vh, non_blocking=True)
-        b.step(qd, kd_, vd, pos, out=out)
-        pos.add_(1)
-        oh.copy_(out, non_blocking=True)
+        stepper.run()
     torch.cuda.synchronize()
     barrier()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     x0.record()
     for _ in range(ke):
-        qd.copy_(qh, non_blocking=True); kd_.copy_(kh, non_blocking=True); vd.copy_(vh, non_blocking=True)
-        b.step(qd, kd_, vd, pos, out=out)
-        pos.add_(1)
-        oh.copy_(out, non_blocking=True)
+        stepper.run()
     x1.record()
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(x0.elapsed_time(x1))
     e2e_value = world * S * ke / (e2e_ms / 1e3)
-    h2d = (q.numel() + k.numel() + v.numel()) * q.element_size()
-    d2h = out.numel() * out.element_size()
+    h2d, d2h = stepper.h2d_bytes, stepper.d2h_bytes
     b.check_device_status()
 
     summ = paged = None
@@ -496,7 +491,8 @@ def main():
                              "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                        "steps": ke, "api": "SessionBatch.step (ic_decode_step) with pinned host buffers"},
+                        "steps": ke, "api": "SessionBatch.host_stepper: pinned q/k/v -> device, ic_decode_step, o -> pinned host, "
+                               "one CUDA graph per step"},
                 "gpu_launches": args.steps * (L + 1),
                 "clocks": sampler.summary() if sampler else None,
                 "cuda_graph": not args.no_graph,

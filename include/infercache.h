@@ -148,6 +148,11 @@ typedef struct ic_decode_args {
   int32_t kernel_variant;  /* ic_decode_variant */
   int32_t pdl;             /* 1: launch with programmatic dependent launch */
   int32_t mass_layers;     /* innermost dimension of mass (>= layer + 1) */
+  float* score_ws;         /* optional device workspace for the lean kernel's
+                              per-slot scores (ic_decode_workspace_floats
+                              floats, 128-byte aligned); NULL keeps them in
+                              shared memory (fewer CTAs per SM) */
+  int64_t score_ws_floats; /* size of score_ws */
 } ic_decode_args;
 
 /* Kernel A implementations.  AUTO picks CUDA cores for fp32 pools; for fp16 /
@@ -430,6 +435,11 @@ typedef struct ic_compact_attn_args {
   int32_t _pad;
 } ic_compact_attn_args;
 int ic_compact_attention(const ic_compact_attn_args* a, void* stream);
+
+/* Floats of score workspace the lean decode kernel uses for `mass_layers`
+ * layers of `num_sessions` sessions (0 for unsupported shapes). */
+int64_t ic_decode_workspace_floats(int32_t mass_layers, int32_t num_sessions, int32_t num_kv_heads,
+                                   int32_t num_q_heads, int32_t budget);
 
 /* ---- library information --------------------------------------------------*/
 const char* ic_status_str(int status);

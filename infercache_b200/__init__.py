@@ -13,7 +13,7 @@ Public API (the reference's names):
 
 Importing the package needs no GPU; constructing a cache does.
 """
-from .hierarchical_cache import CacheConfig, CacheStats, HierarchicalKVCache, SessionBatch  # noqa: F401
+from .hierarchical_cache import CacheConfig, CacheStats, HierarchicalKVCache, HostStepper, SessionBatch  # noqa: F401
 from .paged_cache import (PAGE_SIZE, KVAllocator, MultiSessionCache, PagedCacheConfig,  # noqa: F401
                           PagedSessionView, PagePool)
 from .summary import SummaryScores, attention_mass, summary_score  # noqa: F401

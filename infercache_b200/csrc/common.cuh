@@ -112,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---- bulk copy global -> shared through the TMA engine ---------------------
-// Untiled cp.async.bulk (no multicast): both addresses 16-byte aligned, size a
+// Untiled cp.async.bulk into this CTA only: both addresses 16-byte aligned, size a
 // multiple of 16.  Completion is signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

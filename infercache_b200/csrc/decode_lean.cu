@@ -42,7 +42,6 @@ constexpr int LN_D = 128;
 constexpr int LN_R = 16;                       // rows per chunk
 constexpr int LN_PITCH = LN_D * 2 + 16;        // padded row: conflict-free ldmatrix
 constexpr int LN_STAGE = 2 * LN_R * LN_PITCH;  // K chunk + V chunk
-constexpr int LN_RING = LN_WARPS * 2 * LN_STAGE;
 constexpr float LN_LOG2E = 1.4426950408889634f;
 constexpr float LN_RESCALE = 8.0f;
 
@@ -53,21 +52,32 @@ struct LeanSmem {
   int sc_off, row_off, occ_off, stat_off, total;
 };
 
-__host__ __device__ inline LeanSmem lean_smem(int ntot, int NG) {
+// Scores live in shared memory, or (ws) in a global workspace region of
+// NG * 8 * pitch floats per CTA; a region is a whole number of 128-byte lines.
+__host__ __device__ inline LeanSmem lean_smem(int ntot, int NG, int nstg, bool ws) {
   LeanSmem L;
   L.nch = (ntot + LN_R - 1) / LN_R;
   L.ntp = L.nch * LN_R;
   L.pitch = ln_align(L.ntp, 32) + 4;  // pitch % 32 == 4: conflict-free score stores
-  int o = LN_RING;                    // the merge buffers alias the ring afterwards
+  int o = LN_WARPS * nstg * LN_STAGE; // the merge buffers alias the ring afterwards
   const int merge = LN_WARPS * NG * 8 * (LN_D + 2) * 4;
   if (merge > o) o = merge;
   o = ln_align(o, 128);
-  L.sc_off = o;   o = ln_align(o + NG * 8 * L.pitch * 4, 16);
+  L.sc_off = o;   o = ln_align(o + (ws ? 0 : NG * 8 * L.pitch * 4), 16);
   L.row_off = o;  o = ln_align(o + L.ntp * 4, 16);
   L.occ_off = o;  o = ln_align(o + L.ntp, 16);
   L.stat_off = o; o = ln_align(o + 2 * NG * 8 * 4, 16);
   L.total = o;
   return L;
+}
+
+int64_t lean_workspace_floats(int layers, int S, int Hkv, int Hq, int budget) {
+  if (layers < 1 || S < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv || budget < 1) return 0;
+  const int G = Hq / Hkv;
+  if (G > 16) return 0;
+  const int NG = G <= 8 ? 1 : 2;
+  const LeanSmem L = lean_smem(budget + 1, NG, 2, true);
+  return static_cast<int64_t>(layers) * S * Hkv * NG * 8 * L.pitch;
 }
 
 __device__ __forceinline__ uint32_t movtrans(uint32_t x) {
@@ -87,8 +97,12 @@ __device__ __forceinline__ float fast_ex2(float x) {
   return y;
 }
 
-template <typename T, int NG>
-__global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_decode_args a) {
+__device__ __forceinline__ void discard_l2(const void* p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
+template <typename T, int NG, int NSTG, bool WS>
+__global__ void __launch_bounds__(LN_THREADS, (WS && NG == 1) ? 3 : 2) decode_lean_kernel(const ic_decode_args a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;  // P as high + low bf16
   const int h = blockIdx.x, s = blockIdx.y;
@@ -96,9 +110,12 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   const int g = lane >> 2, tq = lane & 3;
   const int budget = a.tiers.budget, ntot = budget + 1;
   const int Hkv = a.pool.num_kv_heads, Hq = a.num_q_heads, G = Hq / Hkv;
-  const LeanSmem L = lean_smem(ntot, NG);
+  const LeanSmem L = lean_smem(ntot, NG, NSTG, WS);
   const int nch = L.nch, ntp = L.ntp, pitch = L.pitch;
-  float* sc = reinterpret_cast<float*>(smem + L.sc_off);  // [NG*8][pitch] log2-scaled scores
+  // [NG*8][pitch] log2-scaled scores
+  float* sc = WS ? a.score_ws + ((static_cast<size_t>(a.layer) * a.sess.num_sessions + s) * Hkv + h) *
+                                    (static_cast<size_t>(NG) * 8 * pitch)
+                 : reinterpret_cast<float*>(smem + L.sc_off);
   int32_t* rows = reinterpret_cast<int32_t*>(smem + L.row_off);
   uint8_t* occ_s = smem + L.occ_off;
   float* stat = reinterpret_cast<float*>(smem + L.stat_off);  // [NG*8] max, [NG*8] 1 / sum
@@ -171,11 +188,11 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   const int per = (nch + LN_WARPS - 1) / LN_WARPS;
   const int c0 = warp * per;
   const int c1 = min(nch, c0 + per);
-  unsigned char* wring = smem + warp * 2 * LN_STAGE;
+  unsigned char* wring = smem + warp * NSTG * LN_STAGE;
 
   auto issue = [&](int c) {
     if (c < c1) {
-      unsigned char* dk = wring + ((c - c0) & 1) * LN_STAGE;
+      unsigned char* dk = wring + ((c - c0) % NSTG) * LN_STAGE;
       unsigned char* dv = dk + LN_R * LN_PITCH;
       const int v = lane & 15;
 #pragma unroll
@@ -209,12 +226,13 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
     for (int mt = 0; mt < 8; ++mt) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
   }
 
-  issue(c0);
+#pragma unroll
+  for (int i = 0; i < NSTG - 1; ++i) issue(c0 + i);
   for (int c = c0; c < c1; ++c) {
-    issue(c + 1);
-    cp_async_wait<1>();
+    issue(c + NSTG - 1);
+    cp_async_wait<NSTG - 1>();
     __syncwarp();
-    const unsigned char* bk = wring + ((c - c0) & 1) * LN_STAGE;
+    const unsigned char* bk = wring + ((c - c0) % NSTG) * LN_STAGE;
     const unsigned char* bv = bk + LN_R * LN_PITCH;
     const int r0 = c * LN_R;
 
@@ -393,17 +411,22 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
       mcol[static_cast<size_t>(t) * ML] = m;
     }
   }
+  if (WS) {  // the scores are dead: drop their L2 lines without writing them back
+    __syncthreads();
+    const int lines = HS * pitch * 4 / 128;
+    for (int i = tid; i < lines; i += LN_THREADS) discard_l2(sc + i * 32);
+  }
   if (a.pdl) grid_dependency_wait();  // complete only after the previous layer
 }
 
-template <typename T, int NG>
+template <typename T, int NG, int NSTG, bool WS>
 int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
-  const LeanSmem L = lean_smem(a.tiers.budget + 1, NG);
+  const LeanSmem L = lean_smem(a.tiers.budget + 1, NG, NSTG, WS);
   if (L.total > 227 * 1024) {
     set_last_error("decode (lean): budget too large for one CTA's shared memory");
     return IC_ERR_UNSUPPORTED;
   }
-  auto kern = decode_lean_kernel<T, NG>;
+  auto kern = decode_lean_kernel<T, NG, NSTG, WS>;
   static int smem_limit = 0;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -420,6 +443,15 @@ int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
   return launch_status("decode_layer (lean)");
 }
 
+template <typename T, int NG>
+int launch_lean_ws(const ic_decode_args& a, cudaStream_t stream) {
+  const int64_t need = lean_workspace_floats(a.layer + 1, a.sess.num_sessions, a.pool.num_kv_heads,
+                                             a.num_q_heads, a.tiers.budget);
+  const bool ws = a.score_ws && need > 0 && a.score_ws_floats >= need &&
+                  (reinterpret_cast<uintptr_t>(a.score_ws) & 127) == 0;
+  return ws ? launch_lean<T, NG, 2, true>(a, stream) : launch_lean<T, NG, 2, false>(a, stream);
+}
+
 }  // namespace
 
 int launch_decode_lean(const ic_decode_args& a, cudaStream_t stream) {
@@ -429,11 +461,16 @@ int launch_decode_lean(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_UNSUPPORTED;
   }
   if (a.pool.dtype == IC_F16)
-    return G <= 8 ? launch_lean<__half, 1>(a, stream) : launch_lean<__half, 2>(a, stream);
+    return G <= 8 ? launch_lean_ws<__half, 1>(a, stream) : launch_lean_ws<__half, 2>(a, stream);
   if (a.pool.dtype == IC_BF16)
-    return G <= 8 ? launch_lean<__nv_bfloat16, 1>(a, stream) : launch_lean<__nv_bfloat16, 2>(a, stream);
+    return G <= 8 ? launch_lean_ws<__nv_bfloat16, 1>(a, stream) : launch_lean_ws<__nv_bfloat16, 2>(a, stream);
   set_last_error("decode (lean): dtype must be fp16 or bf16");
   return IC_ERR_INVALID_ARG;
 }
 
 }  // namespace ic
+
+extern "C" int64_t ic_decode_workspace_floats(int32_t mass_layers, int32_t num_sessions, int32_t num_kv_heads,
+                                              int32_t num_q_heads, int32_t budget) {
+  return ic::lean_workspace_floats(mass_layers, num_sessions, num_kv_heads, num_q_heads, budget);
+}

@@ -19,6 +19,74 @@ namespace ic {
 
 constexpr int EV_THREADS = 512;
 
+// Importance of slot j after this step's decay and received mass: the slot's
+// mass is MH contiguous columns of ML layers; each column is summed in layer
+// order, then the columns in head order (all loads of a batch issued before
+// its adds), and importance = fl(fl(importance * decay) + fl(sum / div)).
+__device__ __forceinline__ float updated_importance(const ic_evict_args& a, int s, int j, float v) {
+  const int ntot = a.tiers.budget + 1;
+  float add = 0.f;
+  if (a.mass) {
+    const int MH = a.mass_heads, ML = a.mass_layers;
+    const float* base = a.mass + (static_cast<size_t>(s) * MH * ntot + j) * ML;
+    const size_t hstride = static_cast<size_t>(ntot) * ML;
+    float tot = 0.f, acc = 0.f;
+    if ((ML & 3) == 0) {
+      constexpr int NV = 20;  // float4 loads per batch
+      const int per_h = ML / 4, nvec = MH * per_h;
+      for (int v0 = 0; v0 < nvec; v0 += NV) {
+        float4 x[NV];
+#pragma unroll
+        for (int u = 0; u < NV; ++u) {
+          const int vi = v0 + u;
+          x[u] = vi < nvec ? *reinterpret_cast<const float4*>(base + (vi / per_h) * hstride + (vi % per_h) * 4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < NV; ++u) {
+          const int vi = v0 + u;
+          if (vi >= nvec) break;
+          const int hh = vi / per_h, l4 = vi % per_h;
+          const float xs[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc = (l4 == 0 && q == 0) ? xs[q] : __fadd_rn(acc, xs[q]);
+          if (l4 == per_h - 1) tot = hh == 0 ? acc : __fadd_rn(tot, acc);
+        }
+      }
+    } else {
+      for (int hh = 0; hh < MH; ++hh) {
+        const float* m = base + hh * hstride;
+        for (int l0 = 0; l0 < ML; l0 += 8) {
+          float x[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] = l0 + u < ML ? m[l0 + u] : 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (l0 + u < ML) acc = (l0 + u == 0) ? x[u] : __fadd_rn(acc, x[u]);
+        }
+        tot = hh == 0 ? acc : __fadd_rn(tot, acc);
+      }
+    }
+    add = __fdiv_rn(tot, a.mass_div);
+  }
+  return __fadd_rn(__fmul_rn(v, a.decay), add);
+}
+
+// Step one of kernel B spread over the grid: one thread per slot updates the
+// importance of every occupied slot of every session.
+constexpr int IU_THREADS = 128;
+
+__global__ void __launch_bounds__(IU_THREADS) importance_update_kernel(const ic_evict_args a) {
+  const int s = blockIdx.y, j = blockIdx.x * IU_THREADS + threadIdx.x;
+  const int B = a.tiers.budget;
+  grid_dependency_wait();  // the last layer's mass is complete
+  grid_launch_dependents();
+  if (j >= B) return;
+  const size_t o = static_cast<size_t>(s) * B + j;
+  if (a.sess.occupied[o]) a.sess.importance[o] = updated_importance(a, s, j, a.sess.importance[o]);
+}
+
+template <bool REDUCED>
 __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a) {
   extern __shared__ float imp_s[];  // [budget]
   __shared__ float red_v[EV_THREADS / 32];
@@ -43,60 +111,11 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   grid_dependency_wait();
   grid_launch_dependents();
 
-  // 1. decay + boost of every occupied slot
-  const float decay = a.decay;
-  const float div = a.mass_div;
-  const int MH = a.mass_heads, ML = a.mass_layers;
+  // 1. decay + boost of every occupied slot (already applied when REDUCED)
   for (int j = tid; j < B; j += EV_THREADS) {
     float v = imp[j];
-    if (occ[j]) {
-      float add = 0.f;
-      if (a.mass) {
-        // The slot's mass is MH contiguous columns of ML layers.  Sum each
-        // column in layer order, then the columns in head order; all loads of
-        // a batch are issued before its adds.
-        const float* base = a.mass + (static_cast<size_t>(s) * MH * ntot + j) * ML;
-        const size_t hstride = static_cast<size_t>(ntot) * ML;
-        float tot = 0.f, acc = 0.f;
-        if ((ML & 3) == 0) {
-          constexpr int NV = 20;  // float4 loads per batch
-          const int per_h = ML / 4, nvec = MH * per_h;
-          for (int v0 = 0; v0 < nvec; v0 += NV) {
-            float4 x[NV];
-#pragma unroll
-            for (int u = 0; u < NV; ++u) {
-              const int vi = v0 + u;
-              x[u] = vi < nvec ? *reinterpret_cast<const float4*>(base + (vi / per_h) * hstride + (vi % per_h) * 4)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < NV; ++u) {
-              const int vi = v0 + u;
-              if (vi >= nvec) break;
-              const int hh = vi / per_h, l4 = vi % per_h;
-              const float xs[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) acc = (l4 == 0 && q == 0) ? xs[q] : __fadd_rn(acc, xs[q]);
-              if (l4 == per_h - 1) tot = hh == 0 ? acc : __fadd_rn(tot, acc);
-            }
-          }
-        } else {
-          for (int hh = 0; hh < MH; ++hh) {
-            const float* m = base + hh * hstride;
-            for (int l0 = 0; l0 < ML; l0 += 8) {
-              float x[8];
-#pragma unroll
-              for (int u = 0; u < 8; ++u) x[u] = l0 + u < ML ? m[l0 + u] : 0.f;
-#pragma unroll
-              for (int u = 0; u < 8; ++u)
-                if (l0 + u < ML) acc = (l0 + u == 0) ? x[u] : __fadd_rn(acc, x[u]);
-            }
-            tot = hh == 0 ? acc : __fadd_rn(tot, acc);
-          }
-        }
-        add = __fdiv_rn(tot, div);
-      }
-      v = __fadd_rn(__fmul_rn(v, decay), add);
+    if (!REDUCED && occ[j]) {
+      v = updated_importance(a, s, j, v);
       imp[j] = v;
     }
     imp_s[j] = v;
@@ -326,19 +345,35 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
   }
   const size_t smem = static_cast<size_t>(a->tiers.budget) * sizeof(float);
   if (smem > 200 * 1024) { set_last_error("evict_update: budget too large"); return IC_ERR_UNSUPPORTED; }
-  static int smem_limit = 0;
-  if (const int rc = ensure_dynamic_smem(evict_kernel, static_cast<int>(smem), &smem_limit)) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a->sess.num_sessions, 1, 1);
-  cfg.blockDim = dim3(EV_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
+  // With received mass to sum, the per-slot update runs as its own wide
+  // kernel first (the mass columns are the bulk of kernel B's reads); the
+  // per-session decision kernel then starts from the updated importance.
+  const bool split = a->mass != nullptr;
+  static int smem_limit_r = 0, smem_limit_f = 0;
+  int rc = split ? ensure_dynamic_smem(evict_kernel<true>, static_cast<int>(smem), &smem_limit_r)
+                 : ensure_dynamic_smem(evict_kernel<false>, static_cast<int>(smem), &smem_limit_f);
+  if (rc) return rc;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = a->pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = static_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, evict_kernel, *a);
+  if (split) {
+    cfg.gridDim = dim3((a->tiers.budget + IU_THREADS - 1) / IU_THREADS, a->sess.num_sessions, 1);
+    cfg.blockDim = dim3(IU_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cudaLaunchKernelEx(&cfg, importance_update_kernel, *a);
+    if ((rc = launch_status("evict_update (importance)")) != IC_OK) return rc;
+  }
+  cfg.gridDim = dim3(a->sess.num_sessions, 1, 1);
+  cfg.blockDim = dim3(EV_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  if (split)
+    cudaLaunchKernelEx(&cfg, evict_kernel<true>, *a);
+  else
+    cudaLaunchKernelEx(&cfg, evict_kernel<false>, *a);
   return launch_status("evict_update");
 }
 

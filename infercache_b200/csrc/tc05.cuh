@@ -113,7 +113,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// ---- tiled TMA load (no multicast) ----------------------------------------------
+// ---- tiled TMA load into this CTA ------------------------------------------------
 // 3-D box at element coordinates (x, y, z); x * element size must be a
 // multiple of 16 bytes.  Completion is signalled on `bar` as transaction bytes.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {

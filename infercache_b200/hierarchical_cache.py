@@ -45,7 +45,7 @@ from . import _lib
 from .cache_safety import normalise_kv, to_dynamic_cache
 from .paged_cache import PAGE_SIZE, PagedCacheConfig, PagePool
 
-__all__ = ["CacheConfig", "CacheStats", "SessionBatch", "HierarchicalKVCache", "_normalise_past_kv"]
+__all__ = ["CacheConfig", "CacheStats", "SessionBatch", "HostStepper", "HierarchicalKVCache", "_normalise_past_kv"]
 
 
 @dataclass
@@ -148,6 +148,8 @@ class SessionBatch:
         self.scale = cfg.head_dim ** -0.5
         self.cluster_size = 0
         self.kernel_variant = _lib.IC_DECODE_AUTO
+        self._ws: Optional[torch.Tensor] = None  # decode score workspace (per query-head count)
+        self._ws_hq = -1
 
         self._c_tiers = _lib.ic_tiers(cfg.sink_size, cfg.recent_size, cfg.important_size, B)
         self._c_sess = _lib.ic_sessions(num_sessions=S, slot_table=self.slot_table.data_ptr(),
@@ -199,8 +201,23 @@ class SessionBatch:
         _lib.call("ic_decode_layer", d)
         return out
 
+    def reserve_workspace(self, num_q_heads: int) -> None:
+        """Allocate the decode kernel's score workspace for `num_q_heads` query
+        heads (done by the first decode call; call it before capturing a CUDA
+        graph so no allocation happens inside the capture)."""
+        cfg = self.cfg
+        n = _lib.load().ic_decode_workspace_floats(cfg.num_layers, self.num_sessions, cfg.num_kv_heads,
+                                                   num_q_heads, cfg.total_budget)
+        if n > 0 and (self._ws is None or self._ws.numel() < n):
+            self._ws = torch.empty(n, dtype=torch.float32, device=self.device)
+        self._ws_hq = num_q_heads
+
     def _prepare_decode(self, d: "_lib.ic_decode_args", Hq: int) -> None:
         """Set the launch options of one decode call on `d`."""
+        if self._ws_hq != Hq:
+            self.reserve_workspace(Hq)
+        d.score_ws = _lib.ptr(self._ws)
+        d.score_ws_floats = 0 if self._ws is None else self._ws.numel()
         d.num_q_heads = Hq
         d.cluster_size = self.cluster_size
         d.kernel_variant = self.kernel_variant
@@ -260,6 +277,12 @@ class SessionBatch:
         _lib.call("ic_decode_step", st)
         self._keep = pos
         return out
+
+    def host_stepper(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
+                     out_host: torch.Tensor, positions: torch.Tensor) -> "HostStepper":
+        """A decode step from pinned host buffers, captured once as a CUDA graph
+        (see ``HostStepper``)."""
+        return HostStepper(self, q_host, k_host, v_host, out_host, positions)
 
     def _positions_arg(self, positions) -> torch.Tensor:
         if isinstance(positions, torch.Tensor) and positions.device == self.device and positions.dtype == torch.int64:
@@ -406,6 +429,55 @@ class SessionBatch:
             raise _lib.InferCacheError(_lib.IC_ERR_DEVICE_TIMEOUT, "a device-side wait timed out")
         if st & _lib.IC_DEVFLAG_BAD_ROW:
             raise _lib.InferCacheError(_lib.IC_ERR_CORRUPT_TABLE, "slot table or ring state out of range")
+
+
+class HostStepper:
+    """One decode step of every session of a ``SessionBatch`` driven from host
+    memory: copy q / k / v from pinned host buffers, run ``ic_decode_step``
+    (all layers + eviction), copy the output back to a pinned host buffer and
+    advance each session's position by one -- captured once as a CUDA graph,
+    so a step costs one graph launch on the host.
+
+    q_host [L, S, Hq, D], k_host / v_host [L, S, Hkv, D], out_host
+    [L, S, Hq, D] (pinned, the cache dtype); positions int64 [S] on the
+    device (the position of the next decoded token of each session).  Fill the
+    host inputs, call ``run()``, and read ``out_host`` after the stream has
+    synchronised (``run(sync=True)`` does that)."""
+
+    def __init__(self, batch: "SessionBatch", q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
+                 out_host: torch.Tensor, positions: torch.Tensor):
+        for name, t in (("q_host", q_host), ("k_host", k_host), ("v_host", v_host), ("out_host", out_host)):
+            if t.device.type != "cpu" or not t.is_pinned() or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous pinned host tensor")
+        if positions.device != batch.device or positions.dtype != torch.int64 or positions.numel() != batch.num_sessions:
+            raise ValueError("positions must be an int64 [S] tensor on the cache device")
+        self.batch = batch
+        self.q_host, self.k_host, self.v_host, self.out_host = q_host, k_host, v_host, out_host
+        self.positions = positions
+        dev = batch.device
+        self._q = torch.empty(q_host.shape, dtype=q_host.dtype, device=dev)
+        self._k = torch.empty(k_host.shape, dtype=k_host.dtype, device=dev)
+        self._v = torch.empty(v_host.shape, dtype=v_host.dtype, device=dev)
+        self._o = torch.empty(out_host.shape, dtype=out_host.dtype, device=dev)
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in (q_host, k_host, v_host))
+        self.d2h_bytes = out_host.numel() * out_host.element_size()
+        batch.reserve_workspace(q_host.shape[2])
+        self._stream = torch.cuda.Stream(device=dev)
+        self._stream.wait_stream(torch.cuda.current_stream(dev))
+        self.graph = torch.cuda.CUDAGraph()
+        # relaxed: the first launch of each kernel may set its shared-memory limit
+        with torch.cuda.graph(self.graph, stream=self._stream, capture_error_mode="relaxed"):
+            self._q.copy_(q_host, non_blocking=True)
+            self._k.copy_(k_host, non_blocking=True)
+            self._v.copy_(v_host, non_blocking=True)
+            batch.step(self._q, self._k, self._v, positions, out=self._o)
+            positions.add_(1)
+            out_host.copy_(self._o, non_blocking=True)
+
+    def run(self, sync: bool = False) -> None:
+        self.graph.replay()
+        if sync:
+            torch.cuda.current_stream(self.batch.device).synchronize()
 
 
 class HierarchicalKVCache:

@@ -55,3 +55,24 @@ def test_export_import_roundtrip_then_identical_decoding():
     for key in ("positions", "importance", "occupied", "ctrl", "counters"):
         assert torch.equal(getattr(one_a, key), getattr(one_b, key)), key
     one_a.check_device_status()
+
+
+def test_host_stepper_matches_eager_steps():
+    """SessionBatch.host_stepper (pinned host buffers, one CUDA graph per step)
+    produces the same outputs and cache state as eager steps."""
+    a = _batch(3, seed=11)
+    b = _batch(3, seed=11)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(3, 3, 16, 128, generator=g, device="cuda").half()
+    k = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    v = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    pos = torch.full((3,), 500, dtype=torch.int64, device="cuda")
+    oh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    st = b.host_stepper(q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory(), oh, pos)
+    for i in range(20):
+        ref = a.step(q, k, v, torch.full((3,), 500 + i, dtype=torch.int64, device="cuda"))
+        st.run(sync=True)
+        assert torch.equal(oh, ref.cpu())
+    assert int(pos[0]) == 520
+    for key in ("positions", "importance", "occupied", "ctrl", "counters"):
+        assert torch.equal(getattr(a, key), getattr(b, key)), key
