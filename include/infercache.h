@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define IC_ABI_VERSION 1
+#define IC_ABI_VERSION 2
 
 /* Status codes.  The Python layer maps them to the reference's exception
  * types: RuntimeError for exhaustion / cap (paged_cache.py:229, 244),
@@ -118,10 +118,12 @@ typedef struct ic_sessions {
  * For every session s and KV head h: appends k_new/v_new[s, h] into the
  * staging row of layer `layer`, attends the Hq/Hkv query heads of the group
  * over every occupied logical slot plus the new token (scale * q.k, softmax,
- * P.V), writes out[s, h*G + g], and stores the received mass of each slot
- * summed over the group's query heads into mass[s, h, slot, layer] (index
- * `budget` is the new token; the layer index is the innermost dimension, of
- * size mass_layers).
+ * P.V), writes out[s, h*G + g], and folds the received mass of each slot
+ * summed over the group's query heads into mass[s, h, slot] (index `budget`
+ * is the new token): layer 0 stores it, every later layer adds its own after
+ * the previous layer's kernel has completed, so the per-head sum runs in
+ * layer order whatever the launches' overlap.  The first layer of a step must
+ * be layer 0.
  * Replaces: compact_sdp_attention (triton_ops.py:251-287), gather_cache_kv
  * (:107-135), scatter_importance (:148-175), the model attention fed by
  * to_hf_past_key_values (hierarchical_cache.py:297-351, two_pass.py:312-321)
@@ -142,17 +144,11 @@ typedef struct ic_decode_args {
                               launch (ic_decode_step), so a layer may read them
                               before the previous layer finishes; 0: they may
                               come from the immediately preceding kernel */
-  float* mass;             /* [S, Hkv, budget + 1, mass_layers] */
+  float* mass;             /* [S, Hkv, budget + 1] running sum over layers */
   float scale;             /* softmax scale, normally head_dim ** -0.5 */
   int32_t cluster_size;    /* cluster variant: 0 = choose; else 8 or 16 */
   int32_t kernel_variant;  /* ic_decode_variant */
   int32_t pdl;             /* 1: launch with programmatic dependent launch */
-  int32_t mass_layers;     /* innermost dimension of mass (>= layer + 1) */
-  float* score_ws;         /* optional device workspace for the lean kernel's
-                              per-slot scores (ic_decode_workspace_floats
-                              floats, 128-byte aligned); NULL keeps them in
-                              shared memory (fewer CTAs per SM) */
-  int64_t score_ws_floats; /* size of score_ws */
 } ic_decode_args;
 
 /* Kernel A implementations.  AUTO picks CUDA cores for fp32 pools; for fp16 /
@@ -197,7 +193,8 @@ int ic_evict_update(const ic_evict_args* a, void* stream);
  * ignored); layer l reads q + l * q_layer_stride, k_new / v_new +
  * l * kv_layer_stride and writes out + l * out_layer_stride (strides in
  * elements of the respective dtype).  `evict` is then applied with its own
- * fields (normally mass_heads = Hkv, mass_layers = L, mass_div = L * Hkv).
+ * fields (normally the decode mass buffer with mass_heads = Hkv,
+ * mass_layers = 1, mass_div = L * Hkv).
  * Layers are launched with inputs_ready = 1.  The decode loop of
  * _generate_two_pass (two_pass.py:302-336) with the model's per-layer
  * attention and the cache push of one token per session. */
@@ -435,11 +432,6 @@ typedef struct ic_compact_attn_args {
   int32_t _pad;
 } ic_compact_attn_args;
 int ic_compact_attention(const ic_compact_attn_args* a, void* stream);
-
-/* Floats of score workspace the lean decode kernel uses for `mass_layers`
- * layers of `num_sessions` sessions (0 for unsupported shapes). */
-int64_t ic_decode_workspace_floats(int32_t mass_layers, int32_t num_sessions, int32_t num_kv_heads,
-                                   int32_t num_q_heads, int32_t budget);
 
 /* ---- library information --------------------------------------------------*/
 const char* ic_status_str(int status);

@@ -79,8 +79,7 @@ class ic_decode_args(Structure):
     _fields_ = [("pool", ic_pool), ("tiers", ic_tiers), ("sess", ic_sessions), ("layer", c_int32),
                 ("num_q_heads", c_int32), ("q", c_void_p), ("k_new", c_void_p), ("v_new", c_void_p),
                 ("out", c_void_p), ("out_dtype", c_int32), ("inputs_ready", c_int32), ("mass", c_void_p),
-                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32),
-                ("mass_layers", c_int32), ("score_ws", c_void_p), ("score_ws_floats", c_int64)]
+                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32)]
 
 
 class ic_evict_args(Structure):
@@ -189,8 +188,7 @@ ENTRY_POINTS = {
     "ic_argmin_range": ic_argmin_args,
     "ic_compact_attention": ic_compact_attn_args,
 }
-INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error",
-                     "ic_decode_workspace_floats"]
+INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
 
 _LIB = None
 
@@ -216,8 +214,6 @@ def load(path: Path = LIB_PATH):
     lib.ic_device_check.restype = c_int
     lib.ic_last_error.argtypes = []
     lib.ic_last_error.restype = c_char_p
-    lib.ic_decode_workspace_floats.argtypes = [c_int32] * 5
-    lib.ic_decode_workspace_floats.restype = c_int64
     _LIB = lib
     return lib
 

@@ -12,8 +12,8 @@
 //   3. exchanges per-head maxima and then exp-sums with the other CTAs of its
 //      cluster through distributed shared memory, so every probability is
 //      exp(s - m) / l with the exact global m and l;
-//   4. writes the received mass of each slot summed over the group's query
-//      heads into this layer's column of the mass array;
+//   4. adds the received mass of each slot summed over the group's query
+//      heads to the slot's running sum over layers (layer 0 stores it);
 //   5. computes its partial P.V and reduces the partials across the cluster
 //      through DSMEM in a fixed CTA order.
 // No global scratch, no atomics: results are deterministic run to run.
@@ -222,12 +222,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) decode_kernel(const ic_decode_
 
   // -- 4. received mass per slot, summed over the group's heads in order -----
   {
-    const size_t ML = static_cast<size_t>(a.mass_layers);
-    float* mrow = a.mass + ((static_cast<size_t>(s) * Hkv + h) * ntot + t0) * ML + a.layer;
+    // launches of this kernel are serialised, so the previous layer's sum is final
+    float* mrow = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + t0;
     for (int t = tid; t < n; t += DEC_THREADS) {
       float m = 0.f;
       for (int g = 0; g < G; ++g) m += sc[g * cp + t];
-      mrow[static_cast<size_t>(t) * ML] = m;
+      mrow[t] = a.layer == 0 ? m : __fadd_rn(mrow[t], m);
     }
   }
 
@@ -348,7 +348,6 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   if (a->tiers.budget <= 0 || a->tiers.budget != a->tiers.sink_size + a->tiers.recent_size +
                                                      a->tiers.important_size ||
       a->layer < 0 || a->layer >= a->pool.num_layers || a->sess.num_sessions < 0 ||
-      a->mass_layers <= a->layer ||
       a->pool.pool_tokens <= 0 || a->sess.num_sessions > 65535 || Hkv > 65535) {
     set_last_error("decode: bad sizes");
     return IC_ERR_INVALID_ARG;

@@ -17,14 +17,15 @@
 //                   for a bf16 cache.
 // Each chunk's scaled scores go to shared memory; after the four warps'
 // (max, sum, O) are merged, the exact softmax gives every slot's received
-// mass (summed over the group's heads) for this layer's mass column.
+// mass (summed over the group's heads), which the CTA adds to the slot's
+// running sum over layers once the previous layer has completed.
 //
 // The last logical slot is the staging row: its K/V come from k_new / v_new,
 // which the CTA also writes to the pool.  Programmatic dependent launch
 // follows the streaming kernel's protocol: with inputs_ready, layers after
 // the first read nothing another running kernel writes and let the next
-// layer launch at once; a final grid-dependency wait keeps completion in
-// layer order for the eviction kernel.
+// layer launch at once; the grid-dependency wait before the mass fold keeps
+// the sum and completion in layer order for the eviction kernel.
 #include <math.h>
 
 #include <type_traits>
@@ -52,32 +53,21 @@ struct LeanSmem {
   int sc_off, row_off, occ_off, stat_off, total;
 };
 
-// Scores live in shared memory, or (ws) in a global workspace region of
-// NG * 8 * pitch floats per CTA; a region is a whole number of 128-byte lines.
-__host__ __device__ inline LeanSmem lean_smem(int ntot, int NG, int nstg, bool ws) {
+__host__ __device__ inline LeanSmem lean_smem(int ntot, int NG) {
   LeanSmem L;
   L.nch = (ntot + LN_R - 1) / LN_R;
   L.ntp = L.nch * LN_R;
   L.pitch = ln_align(L.ntp, 32) + 4;  // pitch % 32 == 4: conflict-free score stores
-  int o = LN_WARPS * nstg * LN_STAGE; // the merge buffers alias the ring afterwards
-  const int merge = LN_WARPS * NG * 8 * (LN_D + 2) * 4;
+  int o = LN_WARPS * 2 * LN_STAGE;   // the merge buffers and mass alias the ring afterwards
+  const int merge = LN_WARPS * NG * 8 * (LN_D + 2) * 4 + L.ntp * 4;
   if (merge > o) o = merge;
   o = ln_align(o, 128);
-  L.sc_off = o;   o = ln_align(o + (ws ? 0 : NG * 8 * L.pitch * 4), 16);
+  L.sc_off = o;   o = ln_align(o + NG * 8 * L.pitch * 4, 16);
   L.row_off = o;  o = ln_align(o + L.ntp * 4, 16);
   L.occ_off = o;  o = ln_align(o + L.ntp, 16);
   L.stat_off = o; o = ln_align(o + 2 * NG * 8 * 4, 16);
   L.total = o;
   return L;
-}
-
-int64_t lean_workspace_floats(int layers, int S, int Hkv, int Hq, int budget) {
-  if (layers < 1 || S < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv || budget < 1) return 0;
-  const int G = Hq / Hkv;
-  if (G > 16) return 0;
-  const int NG = G <= 8 ? 1 : 2;
-  const LeanSmem L = lean_smem(budget + 1, NG, 2, true);
-  return static_cast<int64_t>(layers) * S * Hkv * NG * 8 * L.pitch;
 }
 
 __device__ __forceinline__ uint32_t movtrans(uint32_t x) {
@@ -97,12 +87,8 @@ __device__ __forceinline__ float fast_ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void discard_l2(const void* p) {
-  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
-}
-
-template <typename T, int NG, int NSTG, bool WS>
-__global__ void __launch_bounds__(LN_THREADS, (WS && NG == 1) ? 3 : 2) decode_lean_kernel(const ic_decode_args a) {
+template <typename T, int NG>
+__global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_decode_args a) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;  // P as high + low bf16
   const int h = blockIdx.x, s = blockIdx.y;
@@ -110,12 +96,9 @@ __global__ void __launch_bounds__(LN_THREADS, (WS && NG == 1) ? 3 : 2) decode_le
   const int g = lane >> 2, tq = lane & 3;
   const int budget = a.tiers.budget, ntot = budget + 1;
   const int Hkv = a.pool.num_kv_heads, Hq = a.num_q_heads, G = Hq / Hkv;
-  const LeanSmem L = lean_smem(ntot, NG, NSTG, WS);
+  const LeanSmem L = lean_smem(ntot, NG);
   const int nch = L.nch, ntp = L.ntp, pitch = L.pitch;
-  // [NG*8][pitch] log2-scaled scores
-  float* sc = WS ? a.score_ws + ((static_cast<size_t>(a.layer) * a.sess.num_sessions + s) * Hkv + h) *
-                                    (static_cast<size_t>(NG) * 8 * pitch)
-                 : reinterpret_cast<float*>(smem + L.sc_off);
+  float* sc = reinterpret_cast<float*>(smem + L.sc_off);  // [NG*8][pitch] log2-scaled scores
   int32_t* rows = reinterpret_cast<int32_t*>(smem + L.row_off);
   uint8_t* occ_s = smem + L.occ_off;
   float* stat = reinterpret_cast<float*>(smem + L.stat_off);  // [NG*8] max, [NG*8] 1 / sum
@@ -188,6 +171,7 @@ __global__ void __launch_bounds__(LN_THREADS, (WS && NG == 1) ? 3 : 2) decode_le
   const int per = (nch + LN_WARPS - 1) / LN_WARPS;
   const int c0 = warp * per;
   const int c1 = min(nch, c0 + per);
+  constexpr int NSTG = 2;
   unsigned char* wring = smem + warp * NSTG * LN_STAGE;
 
   auto issue = [&](int c) {
@@ -345,6 +329,7 @@ __global__ void __launch_bounds__(LN_THREADS, (WS && NG == 1) ? 3 : 2) decode_le
   float* wo = reinterpret_cast<float*>(smem);          // [warp][head][LN_D]
   float* wm = wo + LN_WARPS * HS * LN_D;                // [warp][head]
   float* wl = wm + LN_WARPS * HS;                       // [warp][head]
+  float* ms = wl + LN_WARPS * HS;                       // [ntp] this layer's mass per slot
 #pragma unroll
   for (int nt = 0; nt < NG; ++nt) {
 #pragma unroll
@@ -399,34 +384,29 @@ __global__ void __launch_bounds__(LN_THREADS, (WS && NG == 1) ? 3 : 2) decode_le
   }
   __syncthreads();
   // ---- received mass of every slot, exact softmax, heads in order -------------------
-  {
-    const size_t ML = static_cast<size_t>(a.mass_layers);
-    float* mcol = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot * ML + a.layer;
-    for (int t = tid; t < ntot; t += LN_THREADS) {
-      float m = 0.f;
-      for (int head = 0; head < G; ++head) {
-        const float x = sc[head * pitch + t];
-        if (x != -INFINITY) m += fast_ex2(x - stat[head]) * stat[HS + head];
-      }
-      mcol[static_cast<size_t>(t) * ML] = m;
+  for (int t = tid; t < ntot; t += LN_THREADS) {
+    float m = 0.f;
+    for (int head = 0; head < G; ++head) {
+      const float x = sc[head * pitch + t];
+      if (x != -INFINITY) m += fast_ex2(x - stat[head]) * stat[HS + head];
     }
+    ms[t] = m;
   }
-  if (WS) {  // the scores are dead: drop their L2 lines without writing them back
-    __syncthreads();
-    const int lines = HS * pitch * 4 / 128;
-    for (int i = tid; i < lines; i += LN_THREADS) discard_l2(sc + i * 32);
-  }
-  if (a.pdl) grid_dependency_wait();  // complete only after the previous layer
+  // Fold into the running sum in layer order: after the previous layer has
+  // completed (which also keeps completion in layer order for kernel B).
+  if (a.pdl) grid_dependency_wait();
+  float* macc = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot;
+  for (int t = tid; t < ntot; t += LN_THREADS) macc[t] = a.layer == 0 ? ms[t] : __fadd_rn(macc[t], ms[t]);
 }
 
-template <typename T, int NG, int NSTG, bool WS>
+template <typename T, int NG>
 int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
-  const LeanSmem L = lean_smem(a.tiers.budget + 1, NG, NSTG, WS);
+  const LeanSmem L = lean_smem(a.tiers.budget + 1, NG);
   if (L.total > 227 * 1024) {
     set_last_error("decode (lean): budget too large for one CTA's shared memory");
     return IC_ERR_UNSUPPORTED;
   }
-  auto kern = decode_lean_kernel<T, NG, NSTG, WS>;
+  auto kern = decode_lean_kernel<T, NG>;
   static int smem_limit = 0;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -443,15 +423,6 @@ int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
   return launch_status("decode_layer (lean)");
 }
 
-template <typename T, int NG>
-int launch_lean_ws(const ic_decode_args& a, cudaStream_t stream) {
-  const int64_t need = lean_workspace_floats(a.layer + 1, a.sess.num_sessions, a.pool.num_kv_heads,
-                                             a.num_q_heads, a.tiers.budget);
-  const bool ws = a.score_ws && need > 0 && a.score_ws_floats >= need &&
-                  (reinterpret_cast<uintptr_t>(a.score_ws) & 127) == 0;
-  return ws ? launch_lean<T, NG, 2, true>(a, stream) : launch_lean<T, NG, 2, false>(a, stream);
-}
-
 }  // namespace
 
 int launch_decode_lean(const ic_decode_args& a, cudaStream_t stream) {
@@ -461,16 +432,12 @@ int launch_decode_lean(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_UNSUPPORTED;
   }
   if (a.pool.dtype == IC_F16)
-    return G <= 8 ? launch_lean_ws<__half, 1>(a, stream) : launch_lean_ws<__half, 2>(a, stream);
+    return G <= 8 ? launch_lean<__half, 1>(a, stream) : launch_lean<__half, 2>(a, stream);
   if (a.pool.dtype == IC_BF16)
-    return G <= 8 ? launch_lean_ws<__nv_bfloat16, 1>(a, stream) : launch_lean_ws<__nv_bfloat16, 2>(a, stream);
+    return G <= 8 ? launch_lean<__nv_bfloat16, 1>(a, stream) : launch_lean<__nv_bfloat16, 2>(a, stream);
   set_last_error("decode (lean): dtype must be fp16 or bf16");
   return IC_ERR_INVALID_ARG;
 }
 
 }  // namespace ic
 
-extern "C" int64_t ic_decode_workspace_floats(int32_t mass_layers, int32_t num_sessions, int32_t num_kv_heads,
-                                              int32_t num_q_heads, int32_t budget) {
-  return ic::lean_workspace_floats(mass_layers, num_sessions, num_kv_heads, num_q_heads, budget);
-}

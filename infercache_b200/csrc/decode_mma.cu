@@ -271,12 +271,12 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
 
   // -- 4. received mass per slot, summed over the group's heads in order -------
   {
-    const size_t ML = static_cast<size_t>(a.mass_layers);
-    float* mrow = a.mass + ((static_cast<size_t>(s) * Hkv + h) * ntot + t0) * ML + a.layer;
+    // after this CTA's grid-dependency wait: the previous layer's sum is final
+    float* mrow = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + t0;
     for (int t = tid; t < n; t += MMA_THREADS) {
       float m = 0.f;
       for (int gg = 0; gg < G; ++gg) m += sc[gg * cp + t];
-      mrow[static_cast<size_t>(t) * ML] = m;
+      mrow[t] = a.layer == 0 ? m : __fadd_rn(mrow[t], m);
     }
   }
 

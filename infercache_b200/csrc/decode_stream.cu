@@ -13,7 +13,7 @@
 //     K pass every head's softmax max and sum are exact without any exchange.
 //   Between the passes every thread turns its slots' scores into
 //     p = exp(s - max) / sum, writes each slot's received mass summed over
-//     the heads in order to this layer's mass column, and replaces each score
+//     the heads in order to its running sum over layers, and replaces each score
 //     by a 32-bit word packing p as high and low half-precision parts
 //     (~22 bits of P); the V-pass fragments re-pair the halves by byte permutes.
 //   V stages: O += P . V on the tensor cores.
@@ -23,10 +23,11 @@
 // layer's q / k_new / v_new exist before the step starts) the kernel lets the
 // next layer launch at once and reads nothing another running kernel writes:
 // the slot table and occupancy change only in the eviction kernel, which
-// finished before layer 0 (which waits for it first) let later layers launch,
-// and every layer writes its own mass column.  A final grid-dependency wait
-// keeps completion in layer order, so the eviction kernel that waits on the
-// last layer sees every layer's mass.
+// finished before layer 0 (which waits for it first) let later layers launch.
+// Between the K and V passes the kernel waits for the previous layer before
+// it adds its mass to the running sum, which keeps the sum in layer order and
+// completion in layer order, so the eviction kernel that waits on the last
+// layer sees every layer's mass.
 #include <math.h>
 
 #include "common.cuh"
@@ -210,8 +211,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_stream_kernel(const ic_d
         }
       }
       __syncthreads();
-      const size_t ML = static_cast<size_t>(a.mass_layers);
-      float* mcol = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot * ML + a.layer;
+      // the running mass sum is folded in layer order: wait for the previous
+      // layer here (this also keeps completion in layer order)
+      if (a.pdl) grid_dependency_wait();
+      float* mcol = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot;
       for (int t = tid; t < ntp; t += ST_THREADS) {
         float m = 0.f;
 #pragma unroll
@@ -226,7 +229,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_stream_kernel(const ic_d
           const uint32_t hb = Mma<T>::bits(ps);
           pw[gg * ppad + t] = hb | (static_cast<uint32_t>(Mma<T>::bits(ps - Mma<T>::back(hb))) << 16);
         }
-        if (t < ntot) mcol[static_cast<size_t>(t) * ML] = m;
+        if (t < ntot) mcol[t] = a.layer == 0 ? m : __fadd_rn(mcol[t], m);
       }
       __syncthreads();
     }
@@ -307,7 +310,6 @@ __global__ void __launch_bounds__(ST_THREADS, 1) decode_stream_kernel(const ic_d
         }
       }
   }
-  if (a.pdl) grid_dependency_wait();  // complete only after the previous layer
 }
 
 template <typename T, int GP>

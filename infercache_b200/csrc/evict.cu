@@ -345,10 +345,10 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
   }
   const size_t smem = static_cast<size_t>(a->tiers.budget) * sizeof(float);
   if (smem > 200 * 1024) { set_last_error("evict_update: budget too large"); return IC_ERR_UNSUPPORTED; }
-  // With received mass to sum, the per-slot update runs as its own wide
-  // kernel first (the mass columns are the bulk of kernel B's reads); the
-  // per-session decision kernel then starts from the updated importance.
-  const bool split = a->mass != nullptr;
+  // With many mass columns to sum, the per-slot update runs as its own wide
+  // kernel first (the columns are then the bulk of kernel B's reads); the
+  // per-session decision kernel starts from the updated importance.
+  const bool split = a->mass != nullptr && a->mass_layers >= 8;
   static int smem_limit_r = 0, smem_limit_f = 0;
   int rc = split ? ensure_dynamic_smem(evict_kernel<true>, static_cast<int>(smem), &smem_limit_r)
                  : ensure_dynamic_smem(evict_kernel<false>, static_cast<int>(smem), &smem_limit_f);

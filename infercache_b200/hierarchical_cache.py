@@ -141,15 +141,13 @@ class SessionBatch:
         self.ctrl[:, _lib.IC_CTRL_RECENT_PTR] = cfg.recent_start
         self.counters = torch.zeros((S, _lib.IC_COUNTER_WORDS), dtype=torch.int64, device=dev)
         self.dev_status = torch.zeros(1, dtype=torch.int32, device=dev)
-        # received mass of each slot per KV head and layer (layer innermost)
-        self.mass = torch.zeros((S, cfg.num_kv_heads, ntot, cfg.num_layers), dtype=torch.float32, device=dev)
+        # received mass of each slot per KV head, summed over the step's layers in layer order
+        self.mass = torch.zeros((S, cfg.num_kv_heads, ntot), dtype=torch.float32, device=dev)
         self.events = torch.full((S, 4), -1, dtype=torch.int64, device=dev)
         self._pos_buf = torch.zeros(S, dtype=torch.int64, device=dev)
         self.scale = cfg.head_dim ** -0.5
         self.cluster_size = 0
         self.kernel_variant = _lib.IC_DECODE_AUTO
-        self._ws: Optional[torch.Tensor] = None  # decode score workspace (per query-head count)
-        self._ws_hq = -1
 
         self._c_tiers = _lib.ic_tiers(cfg.sink_size, cfg.recent_size, cfg.important_size, B)
         self._c_sess = _lib.ic_sessions(num_sessions=S, slot_table=self.slot_table.data_ptr(),
@@ -158,9 +156,9 @@ class SessionBatch:
                                         counters=self.counters.data_ptr(), dev_status=self.dev_status.data_ptr())
         self._c_pool = pool.c_pool()
         self._dec = _lib.ic_decode_args(pool=self._c_pool, tiers=self._c_tiers, sess=self._c_sess,
-                                        mass=self.mass.data_ptr(), scale=self.scale, mass_layers=cfg.num_layers)
+                                        mass=self.mass.data_ptr(), scale=self.scale)
         self._ev = _lib.ic_evict_args(tiers=self._c_tiers, sess=self._c_sess, mass=self.mass.data_ptr(),
-                                      mass_heads=cfg.num_kv_heads, mass_layers=cfg.num_layers,
+                                      mass_heads=cfg.num_kv_heads, mass_layers=1,
                                       mass_div=float(cfg.num_layers * cfg.num_kv_heads),
                                       decay=cfg.decay, new_pos=self._pos_buf.data_ptr(),
                                       events=self.events.data_ptr())
@@ -201,23 +199,8 @@ class SessionBatch:
         _lib.call("ic_decode_layer", d)
         return out
 
-    def reserve_workspace(self, num_q_heads: int) -> None:
-        """Allocate the decode kernel's score workspace for `num_q_heads` query
-        heads (done by the first decode call; call it before capturing a CUDA
-        graph so no allocation happens inside the capture)."""
-        cfg = self.cfg
-        n = _lib.load().ic_decode_workspace_floats(cfg.num_layers, self.num_sessions, cfg.num_kv_heads,
-                                                   num_q_heads, cfg.total_budget)
-        if n > 0 and (self._ws is None or self._ws.numel() < n):
-            self._ws = torch.empty(n, dtype=torch.float32, device=self.device)
-        self._ws_hq = num_q_heads
-
     def _prepare_decode(self, d: "_lib.ic_decode_args", Hq: int) -> None:
         """Set the launch options of one decode call on `d`."""
-        if self._ws_hq != Hq:
-            self.reserve_workspace(Hq)
-        d.score_ws = _lib.ptr(self._ws)
-        d.score_ws_floats = 0 if self._ws is None else self._ws.numel()
         d.num_q_heads = Hq
         d.cluster_size = self.cluster_size
         d.kernel_variant = self.kernel_variant
@@ -234,7 +217,7 @@ class SessionBatch:
         e.decay = self.cfg.decay if decay is None else float(decay)
         e.mass = self.mass.data_ptr() if use_mass else 0
         e.mass_heads = self.cfg.num_kv_heads
-        e.mass_layers = self.cfg.num_layers
+        e.mass_layers = 1
         e.mass_div = float(self.cfg.num_layers * self.cfg.num_kv_heads)
         e.pdl = 1 if self.pdl else 0
         _lib.call("ic_evict_update", e)
@@ -461,7 +444,6 @@ class HostStepper:
         self._o = torch.empty(out_host.shape, dtype=out_host.dtype, device=dev)
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in (q_host, k_host, v_host))
         self.d2h_bytes = out_host.numel() * out_host.element_size()
-        batch.reserve_workspace(q_host.shape[2])
         self._stream = torch.cuda.Stream(device=dev)
         self._stream.wait_stream(torch.cuda.current_stream(dev))
         self.graph = torch.cuda.CUDAGraph()

@@ -307,12 +307,17 @@ def test_evict_kernel_ties_exact():
     assert st[0, 7] == rows0[0, 2] and st[0, 2] == rows0[0, B] and st[0, B] == rows0[0, 7]
     assert st[1, 2] == rows0[1, B] and st[1, B] == rows0[1, 2]
     assert b.positions[0, 2].item() == 500 and b.positions[0, 7].item() == 102
-    # decay + mass arithmetic on one session, rounded step by step
+    # decay + mass arithmetic on one session, rounded step by step: the layer
+    # columns [S, Hkv, slot, layer] summed in layer order, then the heads
     g = torch.Generator().manual_seed(2)
-    m = torch.rand(2, 2, B + 1, 3, generator=g)  # [S, Hkv, slot, layer]
-    b.mass.copy_(m)
+    m = torch.rand(2, 2, B + 1, 3, generator=g)
+    mcol = m.to("cuda").contiguous()
     before = b.importance.clone()
-    b.evict([600, 601], decay=0.75)
+    npos = torch.tensor([600, 601], device="cuda")
+    e = _lib.ic_evict_args(tiers=b._c_tiers, sess=b._c_sess, mass=mcol.data_ptr(), mass_heads=2, mass_layers=3,
+                           mass_div=6.0, decay=0.75, pdl=0, new_pos=npos.data_ptr(), events=b.events.data_ptr())
+    _lib.call("ic_evict_update", e)
+    torch.cuda.synchronize()
     mn = m.numpy()
     heads = [((mn[:, hh, :B, 0] + mn[:, hh, :B, 1]) + mn[:, hh, :B, 2]).astype(np.float32) for hh in range(2)]
     want = (before.cpu().numpy() * np.float32(0.75)).astype(np.float32) + \
