@@ -396,7 +396,19 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   // completed (which also keeps completion in layer order for kernel B).
   if (a.pdl) grid_dependency_wait();
   float* macc = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot;
-  for (int t = tid; t < ntot; t += LN_THREADS) macc[t] = a.layer == 0 ? ms[t] : __fadd_rn(macc[t], ms[t]);
+  for (int t0 = 0; t0 < ntot; t0 += 8 * LN_THREADS) {  // all loads of a batch before its stores
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int t = t0 + i * LN_THREADS + tid;
+      x[i] = (a.layer > 0 && t < ntot) ? macc[t] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int t = t0 + i * LN_THREADS + tid;
+      if (t < ntot) macc[t] = a.layer == 0 ? ms[t] : __fadd_rn(x[i], ms[t]);
+    }
+  }
 }
 
 template <typename T, int NG>

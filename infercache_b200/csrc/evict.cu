@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(IU_THREADS) importance_update_kernel(const ic_
 
 template <bool REDUCED>
 __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a) {
-  extern __shared__ float imp_s[];  // [budget]
+  // shared: importance [budget], positions [budget], slot table [budget + 1]
+  extern __shared__ __align__(16) unsigned char ev_smem[];
   __shared__ float red_v[EV_THREADS / 32];
   __shared__ int red_i[EV_THREADS / 32];
   __shared__ int amin_slot;
@@ -96,6 +97,9 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   const int s = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = a.tiers.budget, ntot = B + 1;
+  int64_t* pos_s = reinterpret_cast<int64_t*>(ev_smem);
+  float* imp_s = reinterpret_cast<float*>(pos_s + B);
+  int32_t* stt_s = reinterpret_cast<int32_t*>(imp_s + B);
   const int sink = a.tiers.sink_size, recent = a.tiers.recent_size, cap = a.tiers.important_size;
   const int l2s = sink + recent;
 
@@ -111,8 +115,12 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   grid_dependency_wait();
   grid_launch_dependents();
 
-  // 1. decay + boost of every occupied slot (already applied when REDUCED)
+  // 1. decay + boost of every occupied slot (already applied when REDUCED);
+  // the slot table and positions are staged too, so the decision below reads
+  // shared memory only
+  for (int j = tid; j < ntot; j += EV_THREADS) stt_s[j] = stt[j];
   for (int j = tid; j < B; j += EV_THREADS) {
+    pos_s[j] = pos[j];
     float v = imp[j];
     if (!REDUCED && occ[j]) {
       v = updated_importance(a, s, j, v);
@@ -122,10 +130,14 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   }
   // Snapshot the decision inputs: every thread must branch identically, and
   // thread 0 rewrites ctrl / occupied below.
-  __shared__ int snap_r, snap_fill, snap_disp;
+  __shared__ int snap_r, snap_fill, snap_disp, snap_rf;
+  __shared__ int64_t snap_cnt[IC_COUNTER_WORDS], snap_newpos;
   if (tid == 0) {
     snap_r = ctrl[IC_CTRL_RECENT_PTR];
     snap_fill = ctrl[IC_CTRL_IMPORTANT_FILL];
+    snap_rf = ctrl[IC_CTRL_RECENT_FILL];
+    snap_newpos = a.new_pos[s];
+    for (int i = 0; i < IC_COUNTER_WORDS; ++i) snap_cnt[i] = cnt[i];
     const bool ok = snap_r >= sink && snap_r < l2s && snap_fill >= 0 && snap_fill <= cap;
     if (!ok) {
       if (a.sess.dev_status) atomicOr(a.sess.dev_status, IC_DEVFLAG_BAD_ROW);
@@ -163,13 +175,14 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
     __syncthreads();
   }
 
-  // 3. apply the decision (one thread)
+  // 3. apply the decision (one thread, from the staged copies)
   if (tid == 0) {
     int64_t kind = IC_EV_NONE, dpos = -1, target = -1, epos = -1;
-    const int32_t row_r = stt[r], row_s = stt[B];
+    const int32_t row_r = stt_s[r], row_s = stt_s[B];
     int32_t new_stage = row_r;
+    int64_t evictions = snap_cnt[IC_CNT_EVICTIONS], promotions = snap_cnt[IC_CNT_PROMOTIONS];
     if (displaced) {
-      dpos = pos[r];
+      dpos = pos_s[r];
       int tgt = -1;
       if (score <= 0.f) {
         kind = IC_EV_DROP;
@@ -182,8 +195,8 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
         if (score > imp_s[amin_slot]) {
           tgt = amin_slot;
           kind = IC_EV_EVICT;
-          epos = pos[tgt];
-          cnt[IC_CNT_EVICTIONS] += 1;
+          epos = pos_s[tgt];
+          evictions += 1;
         } else {
           kind = IC_EV_REJECT;
         }
@@ -192,24 +205,26 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
       }
       if (tgt >= 0) {
         target = tgt;
-        new_stage = stt[tgt];
+        new_stage = stt_s[tgt];
         stt[tgt] = row_r;
         pos[tgt] = dpos;
         imp[tgt] = score;
         occ[tgt] = 1;
-        cnt[IC_CNT_PROMOTIONS] += 1;
+        promotions += 1;
       }
     }
     stt[r] = row_s;
     stt[B] = new_stage;
-    pos[r] = a.new_pos[s];
+    pos[r] = snap_newpos;
     imp[r] = 0.f;
     occ[r] = 1;
-    const int rf = ctrl[IC_CTRL_RECENT_FILL];
+    const int rf = snap_rf;
     ctrl[IC_CTRL_RECENT_FILL] = rf + 1 < recent ? rf + 1 : recent;
     ctrl[IC_CTRL_RECENT_PTR] = sink + (r - sink + 1) % recent;
-    cnt[IC_CNT_TOKENS_SEEN] += 1;
-    cnt[IC_CNT_STEPS] += 1;
+    cnt[IC_CNT_TOKENS_SEEN] = snap_cnt[IC_CNT_TOKENS_SEEN] + 1;
+    cnt[IC_CNT_STEPS] = snap_cnt[IC_CNT_STEPS] + 1;
+    cnt[IC_CNT_EVICTIONS] = evictions;
+    cnt[IC_CNT_PROMOTIONS] = promotions;
     if (a.events) {
       int64_t* e = a.events + static_cast<size_t>(s) * 4;
       e[0] = kind; e[1] = dpos; e[2] = target; e[3] = epos;
@@ -343,7 +358,8 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
     set_last_error("evict_update: bad arguments");
     return IC_ERR_INVALID_ARG;
   }
-  const size_t smem = static_cast<size_t>(a->tiers.budget) * sizeof(float);
+  const size_t smem = static_cast<size_t>(a->tiers.budget) * (sizeof(int64_t) + sizeof(float)) +
+                     static_cast<size_t>(a->tiers.budget + 1) * sizeof(int32_t);
   if (smem > 200 * 1024) { set_last_error("evict_update: budget too large"); return IC_ERR_UNSUPPORTED; }
   // With many mass columns to sum, the per-slot update runs as its own wide
   // kernel first (the columns are then the bulk of kernel B's reads); the
