@@ -290,6 +290,70 @@ def paged_leg(device, iters=5):
                          "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
 
 
+C3_WORKLOAD = dict(layers=28, hq=28, hkv=4, d=128, sessions=64, min_prompt=1024, max_prompt=8192, sink=4,
+                   recent=512, important=1532, dtype="float16", decay=0.99, seed=2)
+C3_ALG_BYTES_PER_SESSION_LAYER = 4_227_584  # K/V 4,194,304 + append 2,048 + q/o 14,336 + table 512 + importance 16,384
+
+
+def config3_leg(device, steps=20, warmup=3):
+    """The Qwen2.5-7B-shaped decode: 28 layers, 28/4 heads, head_dim 128,
+    budget 2048 (4/512/1532), 64 sessions primed from prompts of U[1024, 8192]
+    tokens (seed 2), fp16.  A step is one decode step of every session
+    (28 layer launches + kernel B), captured as a CUDA graph; 7.6 GB of K/V
+    per step, far above L2."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    w = C3_WORKLOAD
+    L, Hq, Hkv, D, S = w["layers"], w["hq"], w["hkv"], w["d"], w["sessions"]
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=w["sink"], recent_size=w["recent"],
+                      important_size=w["important"], decay=w["decay"], dtype=torch.float16)
+    b = SessionBatch(cfg, S, device)
+    g = torch.Generator().manual_seed(w["seed"])
+    lens = torch.randint(w["min_prompt"], w["max_prompt"] + 1, (S,), generator=g).tolist()
+    gd = torch.Generator(device=device).manual_seed(w["seed"])
+    for s_, T in enumerate(lens):
+        pk = torch.randn(L, 1, Hkv, T, D, generator=gd, device=device, dtype=torch.float16)
+        pv = torch.randn(L, 1, Hkv, T, D, generator=gd, device=device, dtype=torch.float16)
+        u = torch.rand(T, generator=gd, device=device)
+        b.load_prompt(s_, tuple((pk[l], pv[l]) for l in range(L)), u / u.sum())
+        del pk, pv
+    q = torch.randn(L, S, Hq, D, generator=gd, device=device, dtype=torch.float16)
+    k = torch.randn(L, S, Hkv, D, generator=gd, device=device, dtype=torch.float16)
+    v = torch.randn(L, S, Hkv, D, generator=gd, device=device, dtype=torch.float16)
+    out = torch.empty_like(q)
+    pos = torch.tensor(lens, dtype=torch.int64, device=device)
+    for _ in range(warmup):
+        b.step(q, k, v, pos, out=out)
+        pos.add_(1)
+    torch.cuda.synchronize()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=cap):
+        b.step(q, k, v, pos, out=out)
+        pos.add_(1)
+    for _ in range(warmup):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    b.check_device_status()
+    ms = e0.elapsed_time(e1) / steps
+    alg = S * L * C3_ALG_BYTES_PER_SESSION_LAYER
+    peak, kind = measured_peak()
+    gbs = alg / (ms / 1e3) / 1e9
+    del gr, b, q, k, v, out
+    return {"workload": f"qwen2.5-7b-shaped decode: {S} sessions x {L} layers, {Hq}/{Hkv} heads, head_dim {D}, "
+                        f"budget 2048 (4/512/1532), prompts U[1024, 8192] (seed 2), fp16",
+            "value": S / (ms / 1e3), "unit": "session-tokens/s", "ms_per_step": ms, "steps": steps,
+            "alg_bytes_per_step": alg,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
+
+
 # ---- our arm ----------------------------------------------------------------------------------
 def build_batch(spec, device, seed):
     from infercache_b200 import CacheConfig, SessionBatch
@@ -318,7 +382,8 @@ def main():
     ap.add_argument("--cluster", type=int, default=0)
     ap.add_argument("--no-graph", action="store_true", help="replay steps eagerly instead of as a CUDA graph")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--no-summary", action="store_true", help="skip the summary-pass scorer leg")
+    ap.add_argument("--no-summary", action="store_true",
+                    help="skip the secondary legs (summary scorer, paged gather, 7B-shaped decode)")
     ap.add_argument("--workload", choices=["decode", "summary"], default="decode",
                     help="summary: time only the summary-pass scorer (for profiling)")
     ap.add_argument("--summary-batch", type=int, default=0, help="sequences in the summary workload")
@@ -466,12 +531,14 @@ def main():
     h2d, d2h = stepper.h2d_bytes, stepper.d2h_bytes
     b.check_device_status()
 
-    summ = paged = None
+    summ = paged = c3 = None
     if not args.no_summary:
         log("summary leg")
         summ = summary_leg(device)
         log("paged gather leg")
         paged = paged_leg(device)
+        log("7b-shaped decode leg")
+        c3 = config3_leg(device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -497,7 +564,8 @@ def main():
                 "clocks": sampler.summary() if sampler else None,
                 "cuda_graph": not args.no_graph,
                 "summary_score": summ,
-                "paged_gather": paged}
+                "paged_gather": paged,
+                "decode_7b_shape": c3}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphs

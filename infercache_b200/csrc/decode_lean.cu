@@ -37,8 +37,6 @@
 namespace ic {
 namespace {
 
-constexpr int LN_WARPS = 4;
-constexpr int LN_THREADS = LN_WARPS * 32;
 constexpr int LN_D = 128;
 constexpr int LN_R = 16;                       // rows per chunk
 constexpr int LN_PITCH = LN_D * 2 + 16;        // padded row: conflict-free ldmatrix
@@ -53,13 +51,13 @@ struct LeanSmem {
   int sc_off, row_off, occ_off, stat_off, total;
 };
 
-__host__ __device__ inline LeanSmem lean_smem(int ntot, int NG) {
+__host__ __device__ inline LeanSmem lean_smem(int ntot, int NG, int W) {
   LeanSmem L;
   L.nch = (ntot + LN_R - 1) / LN_R;
   L.ntp = L.nch * LN_R;
   L.pitch = ln_align(L.ntp, 32) + 4;  // pitch % 32 == 4: conflict-free score stores
-  int o = LN_WARPS * 2 * LN_STAGE;   // the merge buffers and mass alias the ring afterwards
-  const int merge = LN_WARPS * NG * 8 * (LN_D + 2) * 4 + L.ntp * 4;
+  int o = W * 2 * LN_STAGE;          // the merge buffers and mass alias the ring afterwards
+  const int merge = W * NG * 8 * (LN_D + 2) * 4 + L.ntp * 4;
   if (merge > o) o = merge;
   o = ln_align(o, 128);
   L.sc_off = o;   o = ln_align(o + NG * 8 * L.pitch * 4, 16);
@@ -87,8 +85,9 @@ __device__ __forceinline__ float fast_ex2(float x) {
   return y;
 }
 
-template <typename T, int NG>
-__global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_decode_args a) {
+template <typename T, int NG, int W>
+__global__ void __launch_bounds__(W * 32, 8 / W) decode_lean_kernel(const ic_decode_args a) {
+  constexpr int NT = W * 32;
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;  // P as high + low bf16
   const int h = blockIdx.x, s = blockIdx.y;
@@ -96,7 +95,7 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   const int g = lane >> 2, tq = lane & 3;
   const int budget = a.tiers.budget, ntot = budget + 1;
   const int Hkv = a.pool.num_kv_heads, Hq = a.num_q_heads, G = Hq / Hkv;
-  const LeanSmem L = lean_smem(ntot, NG);
+  const LeanSmem L = lean_smem(ntot, NG, W);
   const int nch = L.nch, ntp = L.ntp, pitch = L.pitch;
   float* sc = reinterpret_cast<float*>(smem + L.sc_off);  // [NG*8][pitch] log2-scaled scores
   int32_t* rows = reinterpret_cast<int32_t*>(smem + L.row_off);
@@ -135,7 +134,7 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   }
 
   // slot table: pool row per logical slot; -2 = staging row, -1 = padding
-  for (int t = tid; t < ntp; t += LN_THREADS) {
+  for (int t = tid; t < ntp; t += NT) {
     int row = -1;
     uint8_t o = 0;
     if (t < budget) {
@@ -168,7 +167,7 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   __syncthreads();
 
   // this warp's chunks
-  const int per = (nch + LN_WARPS - 1) / LN_WARPS;
+  const int per = (nch + W - 1) / W;
   const int c0 = warp * per;
   const int c1 = min(nch, c0 + per);
   constexpr int NSTG = 2;
@@ -327,9 +326,9 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   __syncthreads();  // the ring is free: merge buffers alias it
   constexpr int HS = NG * 8;
   float* wo = reinterpret_cast<float*>(smem);          // [warp][head][LN_D]
-  float* wm = wo + LN_WARPS * HS * LN_D;                // [warp][head]
-  float* wl = wm + LN_WARPS * HS;                       // [warp][head]
-  float* ms = wl + LN_WARPS * HS;                       // [ntp] this layer's mass per slot
+  float* wm = wo + W * HS * LN_D;                // [warp][head]
+  float* wl = wm + W * HS;                       // [warp][head]
+  float* ms = wl + W * HS;                       // [ntp] this layer's mass per slot
 #pragma unroll
   for (int nt = 0; nt < NG; ++nt) {
 #pragma unroll
@@ -350,14 +349,14 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   __syncthreads();
   {
     const size_t ob = (static_cast<size_t>(s) * Hq + static_cast<size_t>(h) * G) * LN_D;
-    for (int e = tid; e < HS * (LN_D / 8); e += LN_THREADS) {
+    for (int e = tid; e < HS * (LN_D / 8); e += NT) {
       const int head = e / (LN_D / 8), d0 = (e % (LN_D / 8)) * 8;
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < LN_WARPS; ++w) M = fmaxf(M, wm[w * HS + head]);
-      float f[LN_WARPS], Lsum = 0.f;
+      for (int w = 0; w < W; ++w) M = fmaxf(M, wm[w * HS + head]);
+      float f[W], Lsum = 0.f;
 #pragma unroll
-      for (int w = 0; w < LN_WARPS; ++w) {
+      for (int w = 0; w < W; ++w) {
         const float mw = wm[w * HS + head];
         f[w] = mw == -INFINITY ? 0.f : fast_ex2(mw - M);
         Lsum = fmaf(wl[w * HS + head], f[w], Lsum);
@@ -372,7 +371,7 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
         for (int d = d0; d < d0 + 8; ++d) {
           float x = 0.f;
 #pragma unroll
-          for (int w = 0; w < LN_WARPS; ++w) x = fmaf(wo[(w * HS + head) * LN_D + d], f[w], x);
+          for (int w = 0; w < W; ++w) x = fmaf(wo[(w * HS + head) * LN_D + d], f[w], x);
           x *= inv;
           if (a.out_dtype == IC_F32)
             static_cast<float*>(a.out)[ob + static_cast<size_t>(head) * LN_D + d] = x;
@@ -384,7 +383,7 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   }
   __syncthreads();
   // ---- received mass of every slot, exact softmax, heads in order -------------------
-  for (int t = tid; t < ntot; t += LN_THREADS) {
+  for (int t = tid; t < ntot; t += NT) {
     float m = 0.f;
     for (int head = 0; head < G; ++head) {
       const float x = sc[head * pitch + t];
@@ -396,34 +395,29 @@ __global__ void __launch_bounds__(LN_THREADS, 2) decode_lean_kernel(const ic_dec
   // completed (which also keeps completion in layer order for kernel B).
   if (a.pdl) grid_dependency_wait();
   float* macc = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot;
-  for (int t0 = 0; t0 < ntot; t0 += 8 * LN_THREADS) {  // all loads of a batch before its stores
+  for (int t0 = 0; t0 < ntot; t0 += 8 * NT) {  // all loads of a batch before its stores
     float x[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int t = t0 + i * LN_THREADS + tid;
+      const int t = t0 + i * NT + tid;
       x[i] = (a.layer > 0 && t < ntot) ? macc[t] : 0.f;
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int t = t0 + i * LN_THREADS + tid;
+      const int t = t0 + i * NT + tid;
       if (t < ntot) macc[t] = a.layer == 0 ? ms[t] : __fadd_rn(x[i], ms[t]);
     }
   }
 }
 
-template <typename T, int NG>
-int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
-  const LeanSmem L = lean_smem(a.tiers.budget + 1, NG);
-  if (L.total > 227 * 1024) {
-    set_last_error("decode (lean): budget too large for one CTA's shared memory");
-    return IC_ERR_UNSUPPORTED;
-  }
-  auto kern = decode_lean_kernel<T, NG>;
+template <typename T, int NG, int W>
+int launch_one(const ic_decode_args& a, cudaStream_t stream, const LeanSmem& L) {
+  auto kern = decode_lean_kernel<T, NG, W>;
   static int smem_limit = 0;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.pool.num_kv_heads, a.sess.num_sessions, 1);
-  cfg.blockDim = dim3(LN_THREADS, 1, 1);
+  cfg.blockDim = dim3(W * 32, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -433,6 +427,22 @@ int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kern, a);
   return launch_status("decode_layer (lean)");
+}
+
+// Four warp pipelines per CTA when two CTAs fit an SM (the best shape at the
+// 1040-slot budget); eight, one CTA per SM, when the budget's score buffer
+// leaves room for only one.
+template <typename T, int NG>
+int launch_lean(const ic_decode_args& a, cudaStream_t stream) {
+  constexpr int SM_BYTES = 228 * 1024, CTA_RESERVED = 1024;
+  const int ntot = a.tiers.budget + 1;
+  const LeanSmem L4 = lean_smem(ntot, NG, 4);
+  if (2 * (L4.total + CTA_RESERVED) <= SM_BYTES) return launch_one<T, NG, 4>(a, stream, L4);
+  const LeanSmem L8 = lean_smem(ntot, NG, 8);
+  if (L8.total <= 227 * 1024) return launch_one<T, NG, 8>(a, stream, L8);
+  if (L4.total <= 227 * 1024) return launch_one<T, NG, 4>(a, stream, L4);
+  set_last_error("decode (lean): budget too large for one CTA's shared memory");
+  return IC_ERR_UNSUPPORTED;
 }
 
 }  // namespace

@@ -38,10 +38,19 @@ SMALL = {
 }
 
 
+# Wider shapes checked against the oracle only (the oracle is pinned by the
+# SMALL fixtures): the Qwen2.5-7B-shaped budget 2048 (4/512/1532) with 28/4
+# heads on two layers.
+WIDE = {
+    "c3_budget": dict(layers=2, hq=28, hkv=4, d=128, sink=4, recent=512, important=1532, prompt=2600,
+                      steps=8, decay=0.99, dtype="float16", seed=12),
+}
+
+
 def small_inputs(name):
     """Prompt K/V [L, Hkv, T, D], prompt scores [T] (rounded to 0.05 so that
     ties occur), and per-step q [S, L, Hq, D], k/v [S, L, Hkv, D]."""
-    sp = SMALL[name]
+    sp = SMALL[name] if name in SMALL else WIDE[name]
     g = torch.Generator().manual_seed(sp["seed"])
     L, T, S, D = sp["layers"], sp["prompt"], sp["steps"], sp["d"]
     pk = torch.randn(L, sp["hkv"], T, D, generator=g)

@@ -75,7 +75,7 @@ def run_small(name, out_dtype=torch.float32, variant=0, dtype=None):
     variant: kernel A implementation (0 auto, 1 CUDA cores, 2 tensor cores).
     dtype: override the spec's cache dtype ("bfloat16": the oracle then holds
     the bf16-rounded values in float32 storage, which is exact)."""
-    sp = dict(specs.SMALL[name])
+    sp = dict(specs.SMALL[name] if name in specs.SMALL else specs.WIDE[name])
     base_dt = sp["dtype"]
     if dtype is not None:
         sp["dtype"] = dtype

@@ -51,6 +51,14 @@ def test_small_protocol(golden, name):
     cache.batch.check_device_status()
 
 
+@pytest.mark.parametrize("variant", [0, 3])
+def test_wide_budget_vs_oracle(variant):
+    """Budget 2048 (4/512/1532) with 28/4 heads: the lean kernel then runs
+    eight warp pipelines, one CTA per SM (AUTO), and the streaming kernel."""
+    cache, oc, outs, events = run_small("c3_budget", out_dtype=torch.float16, variant=variant)
+    cache.batch.check_device_status()
+
+
 @pytest.mark.parametrize("name", ["f16", "g7"])
 @pytest.mark.parametrize("variant", [1, 2, 3, 4])
 def test_small_protocol_variants(name, variant):

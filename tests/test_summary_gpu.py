@@ -69,6 +69,18 @@ def test_summary_vs_fp32_reference(shape, dtype):
     assert elem_close(res.importance.cpu().numpy(), imp_ref.cpu().numpy(), 1e-3)
 
 
+def test_received_mass_precision():
+    """The received mass is exact fp32 arithmetic up to the exponentials (the
+    exp unit's and the FMA-pipe polynomial's, ~3e-7 relative each): relative
+    2e-5 against the fp32 recomputation from the same bf16 inputs."""
+    from infercache_b200.summary import summary_score
+    q, k, v = rand_qkv(1, 16, 2, 1024, torch.bfloat16, seed=77)
+    res = summary_score(q, k, None, with_output=False)
+    _, _, hm_ref = ref_attention(q, k, v, 128 ** -0.5)
+    torch.cuda.synchronize()
+    assert elem_close(res.head_mass.cpu().numpy(), hm_ref.cpu().numpy(), 2e-5)
+
+
 def test_summary_without_output_matches():
     """out = NULL takes the statistics-only kernel; lse and mass must agree."""
     from infercache_b200.summary import summary_score
