@@ -97,7 +97,7 @@ struct SumParams {
 // ------------------------------------------------------------------------------
 // 1. forward: O and the row log-sum-exp
 // ------------------------------------------------------------------------------
-constexpr int FWD_THREADS = 320;  // producer, MMA, two softmax warpgroups
+constexpr int FWD_THREADS = 192;
 constexpr int FWD_NS = 2;
 constexpr int F_Q = 0;
 constexpr int F_K = TILE;
@@ -105,8 +105,7 @@ constexpr int F_V = F_K + FWD_NS * TILE;
 constexpr int F_P = F_V + FWD_NS * TILE;
 constexpr int F_BAR = F_P + TILE;
 constexpr int F_NBAR = 16;
-constexpr int F_X = F_BAR + F_NBAR * 8 + 16;  // row-max halves [2][2][128], row-sum halves [2][128]
-constexpr int F_BYTES = F_X + 6 * SB * 4 + 1024;  // + alignment slack
+constexpr int F_BYTES = F_BAR + F_NBAR * 8 + 16 + 1024;  // + alignment slack
 
 template <typename T, bool WITH_O>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
@@ -125,8 +124,6 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   uint64_t* p_full = bars + 11;
   uint64_t* pv_done = bars + 12;
   uint64_t* mma_done = bars + 13;
-  uint64_t* mx_bar = bars + 14;  // both halves' row maxima of a tile are in
-  uint64_t* l_bar = bars + 15;   // both halves' row sums are in
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + F_BAR + F_NBAR * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + F_BAR + F_NBAR * 8 + 4);
 
@@ -147,13 +144,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       mbar_init(v_full + i, 1);
       mbar_init(kv_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(s_free + i, 256);
+      mbar_init(s_free + i, 128);
     }
-    mbar_init(p_full, 256);
+    mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
-    mbar_init(mx_bar, 256);
-    mbar_init(l_bar, 256);
     *abort = 0;
     fence_barrier_init();
   }
@@ -225,53 +220,43 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       mbar_wait_bounded(mma_done, 0, p.status);
     }
   } else {
-    // ---- softmax: thread = query row; two warpgroups, each owning 64 of the
-    // row's 128 key columns (and 64 of O's columns) --------------------------------
-    const int half = (warp - 2) >> 2;
+    // ---- softmax warps: thread = query row ------------------------------------
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int cofs = half * 64;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     unsigned char* ps = smem + F_P;
-    float* mx_s = reinterpret_cast<float*>(smem + F_X);  // [parity][half][row]
-    float* l_s = mx_s + 4 * SB;                           // [half][row]
     float m_used = -INFINITY, l = 0.f;
-    float s[64];
+    float s[SB];
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       const int sb = j & 1;
       if (!(ok = warp_wait(s_full + sb, (j >> 1) & 1, p.status, abort))) break;
       tc::fence_after();
-      tc::tmem_ld32(tmem + lane_off + sb * 128 + cofs, s);
-      tc::tmem_ld32(tmem + lane_off + sb * 128 + cofs + 32, s + 32);
+#pragma unroll
+      for (int c = 0; c < SB; c += 32) tc::tmem_ld32(tmem + lane_off + sb * 128 + c, s + c);
       tc::tmem_wait_ld();
       tc::fence_before();
       tc::mbar_arrive(s_free + sb);
 
-      float mh = -INFINITY;
+      float mx = -INFINITY;
       if (j == n - 1) {  // diagonal tile: key c is visible to row r iff c <= r
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          s[c] = cofs + c <= r ? s[c] * p.sl2 : -INFINITY;
-          mh = fmaxf(mh, s[c]);
+        for (int c = 0; c < SB; ++c) {
+          s[c] = c <= r ? s[c] * p.sl2 : -INFINITY;
+          mx = fmaxf(mx, s[c]);
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < SB; ++c) {
           s[c] *= p.sl2;
-          mh = fmaxf(mh, s[c]);
+          mx = fmaxf(mx, s[c]);
         }
       }
-      // the row maximum over both halves
-      mx_s[(sb * 2 + half) * SB + r] = mh;
-      tc::mbar_arrive(mx_bar);
-      if (!(ok = warp_wait(mx_bar, j & 1, p.status, abort))) break;
-      const float mx = fmaxf(mx_s[(sb * 2) * SB + r], mx_s[(sb * 2 + 1) * SB + r]);
       const float m_new = mx > m_used + RESCALE_LOG2 ? mx : m_used;
       const float alpha = m_new == m_used ? 1.f : tc::ex2(m_used - m_new);
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < SB; ++c) {
         s[c] = tc::ex2(s[c] - m_new);
         rs += s[c];
       }
@@ -284,25 +269,25 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           if (__any_sync(0xffffffffu, m_new != m_used)) {
             const float a = m_new != m_used ? alpha : 1.f;
 #pragma unroll 1
-            for (int c = 0; c < 64; c += 32) {
+            for (int c = 0; c < SD; c += 32) {
               float o[32];
-              tc::tmem_ld32(tmem + lane_off + 256 + cofs + c, o);
+              tc::tmem_ld32(tmem + lane_off + 256 + c, o);
               tc::tmem_wait_ld();
 #pragma unroll
               for (int i = 0; i < 32; ++i) o[i] *= a;
-              tc::tmem_st32(tmem + lane_off + 256 + cofs + c, o);
+              tc::tmem_st32(tmem + lane_off + 256 + c, o);
             }
             tc::tmem_wait_st();
           }
         }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < SB / 8; ++q) {
           uint4 w;
           w.x = pack2(s[8 * q + 0], s[8 * q + 1], (T*)nullptr);
           w.y = pack2(s[8 * q + 2], s[8 * q + 3], (T*)nullptr);
           w.z = pack2(s[8 * q + 4], s[8 * q + 5], (T*)nullptr);
           w.w = pack2(s[8 * q + 6], s[8 * q + 7], (T*)nullptr);
-          *reinterpret_cast<uint4*>(ps + sw_chunk(r, half * 8 + q)) = w;
+          *reinterpret_cast<uint4*>(ps + sw_chunk(r, q)) = w;
         }
         fence_proxy_async_smem();
         tc::fence_before();
@@ -312,22 +297,16 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     }
     const int row = qt * SB + r;
     if (ok && WITH_O) ok = warp_wait(pv_done, (n - 1) & 1, p.status, abort);
-    if (ok) {  // the row sum over both halves
-      l_s[half * SB + r] = l;
-      tc::mbar_arrive(l_bar);
-      ok = warp_wait(l_bar, 0, p.status, abort);
-    }
     if (ok) {
       tc::fence_after();
-      const float lt = l_s[r] + l_s[SB + r];
-      if (half == 0 && row < p.T) p.lse[(size_t)bh * p.T + row] = (m_used + log2f(lt)) * LN2;
+      if (row < p.T) p.lse[(size_t)bh * p.T + row] = (m_used + log2f(l)) * LN2;
       if (WITH_O) {
-        const float inv = 1.f / lt;
-        T* orow = reinterpret_cast<T*>(p.out) + ((size_t)bh * p.T + row) * SD + cofs;
+        const float inv = 1.f / l;
+        T* orow = reinterpret_cast<T*>(p.out) + ((size_t)bh * p.T + row) * SD;
 #pragma unroll 1
-        for (int c = 0; c < 64; c += 32) {
+        for (int c = 0; c < SD; c += 32) {
           float o[32];
-          tc::tmem_ld32(tmem + lane_off + 256 + cofs + c, o);
+          tc::tmem_ld32(tmem + lane_off + 256 + c, o);
           tc::tmem_wait_ld();
           if (row < p.T) {
 #pragma unroll
@@ -482,20 +461,15 @@ __global__ void __launch_bounds__(COL_THREADS, 1)
       tc::mbar_arrive(s_free + st);
       const float* ls = lse_s + st * SB;
       float a = 0.f;
-      // every second exponential on the FMA pipe: the exp unit is this loop's limit
       if (t == 0) {  // diagonal tile: query c sees key r iff c >= r
 #pragma unroll
         for (int c = 0; c < SB; ++c) {
-          const float x = fmaf(s[c], p.sl2, -ls[c]);
-          const float e = (c & 1) ? tc::exp2_poly(x) : tc::ex2(x);
+          const float e = tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
           a += c >= r ? e : 0.f;
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < SB; ++c) {
-          const float x = fmaf(s[c], p.sl2, -ls[c]);
-          a += (c & 1) ? tc::exp2_poly(x) : tc::ex2(x);
-        }
+        for (int c = 0; c < SB; ++c) a += tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
       }
       acc += a;
       tc::mbar_arrive(q_empty + st);

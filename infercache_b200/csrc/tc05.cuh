@@ -135,27 +135,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for x <= 0 (results below 2^-126 return 0): split
-// x = j + f with j the nearest integer (|f| <= 1/2) by adding and subtracting
-// 1.5 * 2^23, evaluate 2^f with a degree-5 polynomial, and add j to the
-// exponent field.  The coefficients are a weighted least-squares fit of 2^f on
-// Chebyshev nodes of [-1/2, 1/2] for relative error (maximum relative error
-// 3.5e-7 in fp32 Horner form).  Used to move part of a kernel's
-// exponentials off the multi-function unit.
-__device__ __forceinline__ float exp2_poly(float x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  const float t = x + kShift;
-  const float f = x - (t - kShift);
-  float p = 0.0012915669940412045f;
-  p = fmaf(p, f, 0.009668530896306038f);
-  p = fmaf(p, f, 0.055516887456178665f);
-  p = fmaf(p, f, 0.24022264778614044f);
-  p = fmaf(p, f, 0.6931464672088623f);
-  p = fmaf(p, f, 1.0f);
-  const float y = __int_as_float(__float_as_int(t) * (1 << 23) + __float_as_int(p));
-  return x < -126.0f ? 0.0f : y;
-}
-
 // Named barrier over `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
