@@ -262,7 +262,7 @@ class SessionBatch:
         return out
 
     def host_stepper(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
-                     out_host: torch.Tensor, positions: torch.Tensor) -> "HostStepper":
+                     out_host, positions: torch.Tensor) -> "HostStepper":
         """A decode step from pinned host buffers, captured once as a CUDA graph
         (see ``HostStepper``)."""
         return HostStepper(self, q_host, k_host, v_host, out_host, positions)
@@ -417,49 +417,98 @@ class SessionBatch:
 class HostStepper:
     """One decode step of every session of a ``SessionBatch`` driven from host
     memory: copy q / k / v from pinned host buffers, run ``ic_decode_step``
-    (all layers + eviction), copy the output back to a pinned host buffer and
-    advance each session's position by one -- captured once as a CUDA graph,
-    so a step costs one graph launch on the host.
+    (all layers + eviction), advance each session's position by one and copy
+    the output back to pinned host memory -- the device part captured once as
+    a CUDA graph, so a step costs one graph launch on the host.
 
-    q_host [L, S, Hq, D], k_host / v_host [L, S, Hkv, D], out_host
-    [L, S, Hq, D] (pinned, the cache dtype); positions int64 [S] on the
-    device (the position of the next decoded token of each session).  Fill the
-    host inputs, call ``run()``, and read ``out_host`` after the stream has
-    synchronised (``run(sync=True)`` does that)."""
+    q_host [L, S, Hq, D], k_host / v_host [L, S, Hkv, D] and the output
+    buffers [L, S, Hq, D] are pinned tensors of the cache dtype; positions is
+    an int64 [S] tensor on the device (the position of each session's next
+    decoded token).
+
+    ``out_host`` is one tensor, or a pair for a pipelined stepper: the copy of
+    step i's output to ``out_host[i % 2]`` then runs on a copy stream while
+    step i + 1 computes (a step's inputs are still copied before it starts).
+    ``run()`` returns the index of the buffer receiving this step's output;
+    ``wait(index)`` (or ``synchronize()``) makes it readable."""
 
     def __init__(self, batch: "SessionBatch", q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
-                 out_host: torch.Tensor, positions: torch.Tensor):
-        for name, t in (("q_host", q_host), ("k_host", k_host), ("v_host", v_host), ("out_host", out_host)):
+                 out_host, positions: torch.Tensor):
+        outs = tuple(out_host) if isinstance(out_host, (tuple, list)) else (out_host,)
+        if len(outs) not in (1, 2):
+            raise ValueError("out_host must be a tensor or a pair of tensors")
+        for name, t in (("q_host", q_host), ("k_host", k_host), ("v_host", v_host)) + \
+                tuple((f"out_host[{i}]", o) for i, o in enumerate(outs)):
             if t.device.type != "cpu" or not t.is_pinned() or not t.is_contiguous():
                 raise ValueError(f"{name} must be a contiguous pinned host tensor")
         if positions.device != batch.device or positions.dtype != torch.int64 or positions.numel() != batch.num_sessions:
             raise ValueError("positions must be an int64 [S] tensor on the cache device")
         self.batch = batch
-        self.q_host, self.k_host, self.v_host, self.out_host = q_host, k_host, v_host, out_host
+        self.q_host, self.k_host, self.v_host, self.out_host = q_host, k_host, v_host, outs
         self.positions = positions
+        self.pipelined = len(outs) == 2
         dev = batch.device
         self._q = torch.empty(q_host.shape, dtype=q_host.dtype, device=dev)
         self._k = torch.empty(k_host.shape, dtype=k_host.dtype, device=dev)
         self._v = torch.empty(v_host.shape, dtype=v_host.dtype, device=dev)
-        self._o = torch.empty(out_host.shape, dtype=out_host.dtype, device=dev)
+        self._o = [torch.empty(o.shape, dtype=o.dtype, device=dev) for o in outs]
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in (q_host, k_host, v_host))
-        self.d2h_bytes = out_host.numel() * out_host.element_size()
-        self._stream = torch.cuda.Stream(device=dev)
-        self._stream.wait_stream(torch.cuda.current_stream(dev))
-        self.graph = torch.cuda.CUDAGraph()
-        # relaxed: the first launch of each kernel may set its shared-memory limit
-        with torch.cuda.graph(self.graph, stream=self._stream, capture_error_mode="relaxed"):
-            self._q.copy_(q_host, non_blocking=True)
-            self._k.copy_(k_host, non_blocking=True)
-            self._v.copy_(v_host, non_blocking=True)
-            batch.step(self._q, self._k, self._v, positions, out=self._o)
-            positions.add_(1)
-            out_host.copy_(self._o, non_blocking=True)
+        self.d2h_bytes = outs[0].numel() * outs[0].element_size()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        self.graphs = []
+        for k in range(len(outs)):
+            gr = torch.cuda.CUDAGraph()
+            # relaxed: the first launch of each kernel may set its shared-memory limit
+            with torch.cuda.graph(gr, stream=cap, capture_error_mode="relaxed"):
+                self._q.copy_(q_host, non_blocking=True)
+                self._k.copy_(k_host, non_blocking=True)
+                self._v.copy_(v_host, non_blocking=True)
+                batch.step(self._q, self._k, self._v, positions, out=self._o[k])
+                positions.add_(1)
+                if not self.pipelined:
+                    outs[0].copy_(self._o[0], non_blocking=True)
+            self.graphs.append(gr)
+        self.graph = self.graphs[0]
+        self._copy = torch.cuda.Stream(device=dev)
+        self._computed = [torch.cuda.Event() for _ in outs]
+        self._copied = [torch.cuda.Event() for _ in outs]
+        self._used = [False] * len(outs)
+        self._next = 0
 
-    def run(self, sync: bool = False) -> None:
-        self.graph.replay()
+    def run(self, sync: bool = False) -> int:
+        k = self._next
+        main = torch.cuda.current_stream(self.batch.device)
+        if self.pipelined and self._used[k]:
+            main.wait_event(self._copied[k])  # the device output buffer has been read
+        self.graphs[k].replay()
+        if self.pipelined:
+            self._computed[k].record(main)
+            self._copy.wait_event(self._computed[k])
+            with torch.cuda.stream(self._copy):
+                self.out_host[k].copy_(self._o[k], non_blocking=True)
+            self._copied[k].record(self._copy)
+            self._used[k] = True
+            self._next = 1 - k
         if sync:
+            self.wait(k)
+        return k
+
+    def wait(self, index: int = 0) -> None:
+        """Block the host until out_host[index] holds its step's output."""
+        if self.pipelined:
+            self._copied[index].synchronize()
+        else:
             torch.cuda.current_stream(self.batch.device).synchronize()
+
+    def synchronize(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Make `stream` (default: the current one) wait for every pending
+        output copy, without blocking the host."""
+        st = stream or torch.cuda.current_stream(self.batch.device)
+        if self.pipelined:
+            for k, used in enumerate(self._used):
+                if used:
+                    st.wait_event(self._copied[k])
 
 
 class HierarchicalKVCache:

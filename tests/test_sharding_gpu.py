@@ -76,3 +76,29 @@ def test_host_stepper_matches_eager_steps():
     assert int(pos[0]) == 520
     for key in ("positions", "importance", "occupied", "ctrl", "counters"):
         assert torch.equal(getattr(a, key), getattr(b, key)), key
+
+
+def test_pipelined_host_stepper_matches_eager_steps():
+    """The pipelined stepper (output copies on a copy stream, two host
+    buffers) delivers every step's output intact."""
+    a = _batch(3, seed=13)
+    b = _batch(3, seed=13)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    q = torch.randn(3, 3, 16, 128, generator=g, device="cuda").half()
+    k = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    v = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    pos = torch.full((3,), 700, dtype=torch.int64, device="cuda")
+    ohs = tuple(torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2))
+    st = b.host_stepper(q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory(), ohs, pos)
+    refs = [a.step(q, k, v, torch.full((3,), 700 + i, dtype=torch.int64, device="cuda")).cpu() for i in range(12)]
+    for i in range(12):
+        idx = st.run()
+        assert idx == i % 2
+        if i % 3 == 2:  # read back some steps right away, let others overlap
+            st.wait(idx)
+            assert torch.equal(ohs[idx], refs[i])
+    st.synchronize()
+    torch.cuda.synchronize()
+    assert torch.equal(ohs[1], refs[11]) and torch.equal(ohs[0], refs[10])
+    for key in ("positions", "importance", "occupied", "ctrl", "counters"):
+        assert torch.equal(getattr(a, key), getattr(b, key)), key
