@@ -87,6 +87,7 @@ class CacheStats:
     sink_fill: int = 0
     recent_fill: int = 0
     important_fill: int = 0
+    total_promotions: int = 0  # tokens moved from the recent ring into the importance tier
 
 
 def _check_cfg(cfg: CacheConfig) -> None:
@@ -398,12 +399,32 @@ class SessionBatch:
                                 occupied=self.occupied[s].data_ptr(), ctrl=self.ctrl[s].data_ptr(),
                                 counters=self.counters[s].data_ptr(), dev_status=self.dev_status.data_ptr())
 
-    def stats(self, session: int) -> CacheStats:
-        c = self.ctrl[session].tolist()
-        n = self.counters[session].tolist()
+    @staticmethod
+    def _stats_from(c, n) -> CacheStats:
         sf, rf, imf = c[_lib.IC_CTRL_SINK_FILL], c[_lib.IC_CTRL_RECENT_FILL], c[_lib.IC_CTRL_IMPORTANT_FILL]
         return CacheStats(total_tokens_seen=n[_lib.IC_CNT_TOKENS_SEEN], total_evictions=n[_lib.IC_CNT_EVICTIONS],
-                          current_fill=sf + rf + imf, sink_fill=sf, recent_fill=rf, important_fill=imf)
+                          current_fill=sf + rf + imf, sink_fill=sf, recent_fill=rf, important_fill=imf,
+                          total_promotions=n[_lib.IC_CNT_PROMOTIONS])
+
+    def stats(self, session: int) -> CacheStats:
+        return self._stats_from(self.ctrl[session].tolist(), self.counters[session].tolist())
+
+    def stats_async(self) -> "StatsReadback":
+        """Every session's counters copied to pinned host memory behind the
+        work already queued on the current stream, without synchronising;
+        ``.result()`` waits for the copy and returns one CacheStats per session."""
+        return StatsReadback(self)
+
+    def export_session(self, session: int) -> dict:
+        """One session's complete state (K/V of every slot and layer, positions,
+        importance, occupancy, tier counters) as device tensors."""
+        from .sharding import export_session
+        return export_session(self, session)
+
+    def import_session(self, session: int, state: dict) -> None:
+        """Load a state from ``export_session`` into session row `session`."""
+        from .sharding import import_session
+        import_session(self, session, state)
 
     def check_device_status(self) -> None:
         """Raise if a kernel reported a bounded-wait timeout or a bad row."""
@@ -412,6 +433,25 @@ class SessionBatch:
             raise _lib.InferCacheError(_lib.IC_ERR_DEVICE_TIMEOUT, "a device-side wait timed out")
         if st & _lib.IC_DEVFLAG_BAD_ROW:
             raise _lib.InferCacheError(_lib.IC_ERR_CORRUPT_TABLE, "slot table or ring state out of range")
+
+
+class StatsReadback:
+    """Asynchronous copy of a SessionBatch's control words and counters."""
+
+    def __init__(self, batch: "SessionBatch"):
+        self._ctrl = torch.empty(batch.ctrl.shape, dtype=batch.ctrl.dtype).pin_memory()
+        self._cnt = torch.empty(batch.counters.shape, dtype=batch.counters.dtype).pin_memory()
+        self._ctrl.copy_(batch.ctrl, non_blocking=True)
+        self._cnt.copy_(batch.counters, non_blocking=True)
+        self._event = torch.cuda.Event()
+        self._event.record(torch.cuda.current_stream(batch.device))
+
+    def ready(self) -> bool:
+        return self._event.query()
+
+    def result(self) -> List[CacheStats]:
+        self._event.synchronize()
+        return [SessionBatch._stats_from(c, n) for c, n in zip(self._ctrl.tolist(), self._cnt.tolist())]
 
 
 class HostStepper:
@@ -611,6 +651,15 @@ class HierarchicalKVCache:
 
     def reset(self) -> None:
         self._b.reset([0], zero_kv=True)
+
+    def state_dict(self) -> dict:
+        """The cache's complete state on the host (K/V of every slot and layer,
+        positions, importance, occupancy, tier pointers and counters), so a
+        session can be saved with torch.save and restored later or elsewhere."""
+        return {k: v.cpu() for k, v in self._b.export_session(0).items()}
+
+    def load_state_dict(self, state: dict) -> None:
+        self._b.import_session(0, state)
 
 
 def _normalise_past_kv(past_key_values):

@@ -50,7 +50,7 @@ WIDE = {
 def small_inputs(name):
     """Prompt K/V [L, Hkv, T, D], prompt scores [T] (rounded to 0.05 so that
     ties occur), and per-step q [S, L, Hq, D], k/v [S, L, Hkv, D]."""
-    sp = SMALL[name] if name in SMALL else WIDE[name]
+    sp = name if isinstance(name, dict) else (SMALL[name] if name in SMALL else WIDE[name])
     g = torch.Generator().manual_seed(sp["seed"])
     L, T, S, D = sp["layers"], sp["prompt"], sp["steps"], sp["d"]
     pk = torch.randn(L, sp["hkv"], T, D, generator=g)

@@ -75,13 +75,13 @@ def run_small(name, out_dtype=torch.float32, variant=0, dtype=None):
     variant: kernel A implementation (0 auto, 1 CUDA cores, 2 tensor cores).
     dtype: override the spec's cache dtype ("bfloat16": the oracle then holds
     the bf16-rounded values in float32 storage, which is exact)."""
-    sp = dict(specs.SMALL[name] if name in specs.SMALL else specs.WIDE[name])
+    sp = dict(name if isinstance(name, dict) else (specs.SMALL[name] if name in specs.SMALL else specs.WIDE[name]))
     base_dt = sp["dtype"]
     if dtype is not None:
         sp["dtype"] = dtype
     dt = TORCH_DT[sp["dtype"]]
     rtol = 1e-5 if sp["dtype"] == "float32" else 1e-3
-    pk, pv, scores, q, k, v = specs.small_inputs(name)
+    pk, pv, scores, q, k, v = specs.small_inputs(name if not isinstance(name, dict) else sp)
     if dtype is not None and dtype != base_dt:
         pk, pv, q, k, v = (t.to(dt).float() for t in (pk, pv, q, k, v))
     cache = make_gpu_cache(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"], dt,

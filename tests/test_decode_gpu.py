@@ -375,3 +375,22 @@ def test_paged_trace_gpu(golden):
         assert pages == json.loads(str(g["pages"][i])), (i, op)
         assert abs(msc.utilization() - float(g["util"][i])) < 1e-12
     assert np.array_equal(np.concatenate(gathers), g["gathers"])
+
+
+def _random_spec(i):
+    r = np.random.default_rng(1000 + i)
+    hkv = int(r.integers(1, 3))
+    return dict(layers=int(r.integers(1, 3)), hq=hkv * int(r.integers(1, 9)), hkv=hkv, d=128,
+                sink=int(r.integers(0, 5)), recent=int(r.integers(1, 13)), important=int(r.integers(1, 21)),
+                prompt=int(r.integers(1, 61)), steps=30, decay=float(r.choice([0.99, 0.9, 1.0])),
+                dtype=["float32", "float16"][i % 2], seed=2000 + i)
+
+
+@pytest.mark.parametrize("i", range(12))
+def test_random_small_configs_vs_oracle(i):
+    """Small random tier geometries (empty sink, ring of one, importance tier
+    of one, prompts shorter than the budget, ties in the prompt scores, decay 1)
+    through the fused step: events exact, outputs and importance within the
+    dtype's tolerance, every step."""
+    cache, oc, outs, events = run_small(_random_spec(i), out_dtype=torch.float32)
+    cache.batch.check_device_status()

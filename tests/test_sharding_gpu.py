@@ -102,3 +102,30 @@ def test_pipelined_host_stepper_matches_eager_steps():
     assert torch.equal(ohs[1], refs[11]) and torch.equal(ohs[0], refs[10])
     for key in ("positions", "importance", "occupied", "ctrl", "counters"):
         assert torch.equal(getattr(a, key), getattr(b, key)), key
+
+
+def test_state_dict_round_trip_and_async_stats():
+    """HierarchicalKVCache.state_dict / load_state_dict through host memory,
+    and the asynchronous stats readback."""
+    import io
+    from infercache_b200 import CacheConfig, HierarchicalKVCache
+    cfg = CacheConfig(num_layers=2, num_kv_heads=2, head_dim=128, sink_size=2, recent_size=6, important_size=9,
+                      dtype=torch.float16)
+    a = HierarchicalKVCache(cfg, "cuda:0")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    pkv = tuple((torch.randn(1, 2, 40, 128, generator=g, device="cuda").half(),
+                 torch.randn(1, 2, 40, 128, generator=g, device="cuda").half()) for _ in range(2))
+    a.load_from_hf_output(pkv, torch.rand(40, generator=g, device="cuda"))
+    for i in range(15):
+        a.step(torch.randn(2, 8, 128, generator=g, device="cuda").half(),
+               torch.randn(2, 2, 128, generator=g, device="cuda").half(),
+               torch.randn(2, 2, 128, generator=g, device="cuda").half(), 40 + i)
+    buf = io.BytesIO()
+    torch.save(a.state_dict(), buf)
+    b = HierarchicalKVCache(cfg, "cuda:0")
+    b.load_state_dict(torch.load(io.BytesIO(buf.getvalue())))
+    assert torch.equal(a.positions, b.positions) and torch.equal(a.importance, b.importance)
+    assert torch.equal(a.occupied, b.occupied) and torch.equal(a.K, b.K) and torch.equal(a.V, b.V)
+    assert a.stats == b.stats
+    rb = a.batch.stats_async()
+    assert rb.result()[0] == a.stats
