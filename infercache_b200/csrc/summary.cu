@@ -98,13 +98,14 @@ struct SumParams {
 // 1. forward: O and the row log-sum-exp
 // ------------------------------------------------------------------------------
 constexpr int FWD_THREADS = 192;
-constexpr int FWD_NS = 2;
+constexpr int FWD_KS = 3;  // K ring: a K tile is free once its Q K^T is done
+constexpr int FWD_VS = 2;  // V ring: a V tile is free once its P V is done
 constexpr int F_Q = 0;
 constexpr int F_K = TILE;
-constexpr int F_V = F_K + FWD_NS * TILE;
-constexpr int F_P = F_V + FWD_NS * TILE;
+constexpr int F_V = F_K + FWD_KS * TILE;
+constexpr int F_P = F_V + FWD_VS * TILE;
 constexpr int F_BAR = F_P + TILE;
-constexpr int F_NBAR = 16;
+constexpr int F_NBAR = 20;
 constexpr int F_BYTES = F_BAR + F_NBAR * 8 + 16 + 1024;  // + alignment slack
 
 template <typename T, bool WITH_O>
@@ -116,14 +117,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   const uint32_t sbase = smem_addr(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_free = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* pv_done = bars + 12;
-  uint64_t* mma_done = bars + 13;
+  uint64_t* k_full = bars + 1;    // [3]
+  uint64_t* k_empty = bars + 4;   // [3]
+  uint64_t* v_full = bars + 7;    // [2]
+  uint64_t* v_empty = bars + 9;   // [2]
+  uint64_t* s_full = bars + 11;   // [2]
+  uint64_t* s_free = bars + 13;   // [2]
+  uint64_t* p_full = bars + 15;
+  uint64_t* pv_done = bars + 16;
+  uint64_t* mma_done = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + F_BAR + F_NBAR * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + F_BAR + F_NBAR * 8 + 4);
 
@@ -139,10 +141,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < FWD_KS; ++i) {
       mbar_init(k_full + i, 1);
+      mbar_init(k_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(v_full + i, 1);
-      mbar_init(kv_empty + i, 1);
+      mbar_init(v_empty + i, 1);
       mbar_init(s_full + i, 1);
       mbar_init(s_free + i, 128);
     }
@@ -159,31 +164,36 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   const uint32_t tmem = *tmem_slot;  // S0: +0, S1: +128, O: +256
 
   if (warp == 0) {
-    // ---- TMA producer -------------------------------------------------------
+    // ---- TMA producers: lane 0 streams Q and the K tiles, lane 1 the V tiles ----
     if (lane == 0) {
       int issued = 0;
       mbar_arrive_expect_tx(q_full, TILE);
       tc::tma_load_3d(smem + F_Q, &tq, 0, qt * SB, bh, q_full);
       tc::tma_load_3d(smem + F_Q + SUB, &tq, 64, qt * SB, bh, q_full);
       for (int j = 0; j < n; ++j) {
-        const int st = j % FWD_NS;
-        if (j >= FWD_NS && !one_wait(kv_empty + st, ((j / FWD_NS) - 1) & 1, p.status, abort)) break;
+        const int st = j % FWD_KS;
+        if (j >= FWD_KS && !one_wait(k_empty + st, ((j / FWD_KS) - 1) & 1, p.status, abort)) break;
         mbar_arrive_expect_tx(k_full + st, TILE);
         tc::tma_load_3d(smem + F_K + st * TILE, &tk, 0, j * SB, kvz, k_full + st);
         tc::tma_load_3d(smem + F_K + st * TILE + SUB, &tk, 64, j * SB, kvz, k_full + st);
-        if (WITH_O) {
-          mbar_arrive_expect_tx(v_full + st, TILE);
-          tc::tma_load_3d(smem + F_V + st * TILE, &tv, 0, j * SB, kvz, v_full + st);
-          tc::tma_load_3d(smem + F_V + st * TILE + SUB, &tv, 64, j * SB, kvz, v_full + st);
-        }
         issued = j + 1;
       }
       // drain: every issued load has landed before the CTA may exit
       mbar_wait_bounded(q_full, 0, p.status, 200000000ull);
-      for (int j = issued - FWD_NS < 0 ? 0 : issued - FWD_NS; j < issued; ++j) {
-        mbar_wait_bounded(k_full + j % FWD_NS, (j / FWD_NS) & 1, p.status, 200000000ull);
-        if (WITH_O) mbar_wait_bounded(v_full + j % FWD_NS, (j / FWD_NS) & 1, p.status, 200000000ull);
+      for (int j = issued - FWD_KS < 0 ? 0 : issued - FWD_KS; j < issued; ++j)
+        mbar_wait_bounded(k_full + j % FWD_KS, (j / FWD_KS) & 1, p.status, 200000000ull);
+    } else if (lane == 1 && WITH_O) {
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int st = j % FWD_VS;
+        if (j >= FWD_VS && !one_wait(v_empty + st, ((j / FWD_VS) - 1) & 1, p.status, abort)) break;
+        mbar_arrive_expect_tx(v_full + st, TILE);
+        tc::tma_load_3d(smem + F_V + st * TILE, &tv, 0, j * SB, kvz, v_full + st);
+        tc::tma_load_3d(smem + F_V + st * TILE + SUB, &tv, 64, j * SB, kvz, v_full + st);
+        issued = j + 1;
       }
+      for (int j = issued - FWD_VS < 0 ? 0 : issued - FWD_VS; j < issued; ++j)
+        mbar_wait_bounded(v_full + j % FWD_VS, (j / FWD_VS) & 1, p.status, 200000000ull);
     }
   } else if (warp == 1) {
     // ---- MMA issuer -----------------------------------------------------------
@@ -191,20 +201,20 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       const uint32_t sq = sbase + F_Q, sp = sbase + F_P;
       auto issue_pv = [&](int t) -> bool {
         if (!one_wait(p_full, t & 1, p.status, abort)) return false;
-        if (!one_wait(v_full + t % FWD_NS, (t / FWD_NS) & 1, p.status, abort)) return false;
+        if (!one_wait(v_full + t % FWD_VS, (t / FWD_VS) & 1, p.status, abort)) return false;
         tc::fence_after();
-        const uint32_t sv = sbase + F_V + (t % FWD_NS) * TILE;
+        const uint32_t sv = sbase + F_V + (t % FWD_VS) * TILE;
 #pragma unroll
         for (int kk = 0; kk < SB / 16; ++kk)
           tc::mma_ss(tmem + 256, kdesc(sp, kk), mndesc(sv, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
         tc::commit(pv_done);
-        tc::commit(kv_empty + t % FWD_NS);
+        tc::commit(v_empty + t % FWD_VS);
         return true;
       };
       bool ok = one_wait(q_full, 0, p.status, abort);
       for (int j = 0; ok && j < n; ++j) {
-        const int st = j % FWD_NS, sb = j & 1;
-        if (!one_wait(k_full + st, (j / FWD_NS) & 1, p.status, abort)) break;
+        const int st = j % FWD_KS, sb = j & 1;
+        if (!one_wait(k_full + st, (j / FWD_KS) & 1, p.status, abort)) break;
         if (j >= 2 && !one_wait(s_free + sb, ((j - 2) >> 1) & 1, p.status, abort)) break;
         tc::fence_after();
         const uint32_t sk = sbase + F_K + st * TILE;
@@ -212,7 +222,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         for (int kk = 0; kk < SD / 16; ++kk)
           tc::mma_ss(tmem + sb * 128, kdesc(sq, kk), kdesc(sk, kk), IDESC, kk > 0 ? 1u : 0u);
         tc::commit(s_full + sb);
-        if (!WITH_O) tc::commit(kv_empty + st);
+        tc::commit(k_empty + st);
         if (WITH_O && j >= 1) ok = issue_pv(j - 1);
       }
       if (WITH_O && ok && !*abort) issue_pv(n - 1);
