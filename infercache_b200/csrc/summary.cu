@@ -248,29 +248,28 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       tc::fence_before();
       tc::mbar_arrive(s_free + sb);
 
-      float mx = -INFINITY;
+      // raw row maximum with eight independent chains (the scale is positive,
+      // so scaling the maximum equals the maximum of the scaled scores)
       if (j == n - 1) {  // diagonal tile: key c is visible to row r iff c <= r
 #pragma unroll
-        for (int c = 0; c < SB; ++c) {
-          s[c] = c <= r ? s[c] * p.sl2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < SB; ++c) {
-          s[c] *= p.sl2;
-          mx = fmaxf(mx, s[c]);
-        }
+        for (int c = 0; c < SB; ++c) s[c] = c <= r ? s[c] : -INFINITY;
       }
+      float m8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < SB; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.sl2;
       const float m_new = mx > m_used + RESCALE_LOG2 ? mx : m_used;
       const float alpha = m_new == m_used ? 1.f : tc::ex2(m_used - m_new);
-      float rs = 0.f;
+      float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < SB; ++c) {
-        s[c] = tc::ex2(s[c] - m_new);
-        rs += s[c];
+        s[c] = tc::ex2(fmaf(s[c], p.sl2, -m_new));
+        r4[c & 3] += s[c];
       }
-      l = l * alpha + rs;
+      l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
       if (WITH_O) {
         // P buffer and O are free once the previous P . V has completed
         if (j >= 1) {
@@ -470,18 +469,18 @@ __global__ void __launch_bounds__(COL_THREADS, 1)
       tc::fence_before();
       tc::mbar_arrive(s_free + st);
       const float* ls = lse_s + st * SB;
-      float a = 0.f;
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains, summed in a fixed order
       if (t == 0) {  // diagonal tile: query c sees key r iff c >= r
 #pragma unroll
         for (int c = 0; c < SB; ++c) {
           const float e = tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
-          a += c >= r ? e : 0.f;
+          a4[c & 3] += c >= r ? e : 0.f;
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < SB; ++c) a += tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
+        for (int c = 0; c < SB; ++c) a4[c & 3] += tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
       }
-      acc += a;
+      acc += (a4[0] + a4[1]) + (a4[2] + a4[3]);
       tc::mbar_arrive(q_empty + st);
     }
     // group 1 hands its partial to group 0, which adds it in a fixed order
