@@ -5,12 +5,12 @@
 // two_pass.py:104-137), after materialising P [H, T, T].  Here two kernels
 // stream the causal triangle in 128 x 128 tiles and never store P:
 //
-//  1. summary_fwd_kernel, one CTA per (sequence, query head, 128-row query
-//     tile): S = Q K^T into TMEM (tcgen05.mma, operands staged by TMA), the
-//     row softmax in registers (one thread per row, online max kept unless it
-//     grows by more than 2^8, so O is rescaled only then), P written as
-//     16-bit to shared memory, O += P V into TMEM; epilogue O / l and the row
-//     log-sum-exp.
+//  1. summary_fwd_kernel, one CTA per (sequence, query head, pair of 128-row
+//     query tiles): S = Q K^T into TMEM (tcgen05.mma, operands staged by
+//     TMA), the row softmax in registers (one warpgroup per query tile, one
+//     thread per row, online max kept unless it grows by more than 2^8, so O
+//     is rescaled only then), P written as 16-bit to shared memory, O += P V
+//     into TMEM; epilogue O / l and the row log-sum-exp.
 //  2. summary_colsum_kernel, one CTA per (sequence, query head, 128-key
 //     tile): S^T = K Q^T into TMEM for every query tile at or below the
 //     diagonal, then p = exp2(s * scale * log2 e - lse2) with one thread per
@@ -20,8 +20,8 @@
 //     normalised importance with a fixed-shape block reduction.
 //
 // Roles inside a CTA: warp 0 issues TMA loads, warp 1 owns TMEM and issues
-// the MMAs (one thread), the remaining warps move data between TMEM and
-// registers.  Every mbarrier wait is bounded; on timeout the CTA sets
+// the MMAs (one thread; the forward kernel hands P V to a second issuing
+// warp), the remaining warps move data between TMEM and registers.  Every mbarrier wait is bounded; on timeout the CTA sets
 // IC_DEVFLAG_TIMEOUT, stops issuing work, waits (bounded) for its own
 // in-flight MMAs, frees TMEM and exits.
 #include <cuda.h>
@@ -52,12 +52,6 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
 __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Byte offset of 16-byte chunk `q` (columns 8q .. 8q+7) of row `r` in a
-// 128-column K-major tile stored as two 128-byte-swizzled sub-tiles.
-__device__ __forceinline__ uint32_t sw_chunk(int r, int q) {
-  return (uint32_t)((q >> 3) * SUB + r * 128 + (((q & 7) ^ (r & 7)) << 4));
 }
 
 // K-major descriptor for K step kk (16 elements) of a 128-row tile.
@@ -97,14 +91,25 @@ struct SumParams {
 // ------------------------------------------------------------------------------
 // 1. forward: O and the row log-sum-exp
 // ------------------------------------------------------------------------------
-constexpr int FWD_THREADS = 192;
-constexpr int FWD_KS = 3;  // K ring: a K tile is free once its Q K^T is done
-constexpr int FWD_VS = 2;  // V ring: a V tile is free once its P V is done
-constexpr int F_Q = 0;
-constexpr int F_K = TILE;
-constexpr int F_V = F_K + FWD_KS * TILE;
-constexpr int F_P = F_V + FWD_VS * TILE;
-constexpr int F_BAR = F_P + TILE;
+// One CTA per (sequence, query head, pair of 128-row query tiles qa = 2i,
+// qb = 2i + 1).  Both tiles share every K / V tile they read; one softmax
+// warpgroup per query tile.  The score tiles take turns in one TMEM buffer
+// (S_a(0), S_b(0), S_a(1), ...): each softmax copies its S tile to registers
+// at once, so the next Q K^T starts while it exponentiates.  P goes back to
+// TMEM as 16-bit pairs and P V reads it there (tcgen05.mma with A in TMEM),
+// so P never touches shared memory, whose bandwidth the tensor-core operand
+// reads and the TMA writes already use.  Q K^T and P V are issued by two
+// threads in different warps, so a blocked issue or wait on one side never
+// holds back the other.
+// TMEM columns: S 0, P_a 128, P_b 192, O_a 256, O_b 384.
+// K and V tiles stream through one ring in consumption order K0 K1 V0 K2 V1
+// ... V(n-1) (K one tile ahead); a K slot is released once both tiles'
+// Q K^T are done, a V slot once both P V are done.
+constexpr int FWD_THREADS = 352;  // producer, Q K^T issuer, two softmax warpgroups, P V issuer
+constexpr int FWD_RS = 5;         // K / V ring slots
+constexpr int F_Q = 0;            // Q_a, Q_b
+constexpr int F_R = 2 * TILE;
+constexpr int F_BAR = F_R + FWD_RS * TILE;
 constexpr int F_NBAR = 20;
 constexpr int F_BYTES = F_BAR + F_NBAR * 8 + 16 + 1024;  // + alignment slack
 
@@ -112,48 +117,51 @@ template <typename T, bool WITH_O>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     summary_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const SumParams p) {
+  constexpr int LPS = WITH_O ? 2 : 1;  // ring loads per key step
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
   const uint32_t sbase = smem_addr(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [3]
-  uint64_t* k_empty = bars + 4;   // [3]
-  uint64_t* v_full = bars + 7;    // [2]
-  uint64_t* v_empty = bars + 9;   // [2]
-  uint64_t* s_full = bars + 11;   // [2]
-  uint64_t* s_free = bars + 13;   // [2]
-  uint64_t* p_full = bars + 15;
-  uint64_t* pv_done = bars + 16;
-  uint64_t* mma_done = bars + 17;
+  uint64_t* r_full = bars + 1;    // [FWD_RS]
+  uint64_t* r_empty = bars + 6;   // [FWD_RS]
+  uint64_t* s_full = bars + 11;   // [2]: tile a, tile b
+  uint64_t* s_free = bars + 13;   // the S buffer has been copied out
+  uint64_t* p_full = bars + 14;   // [2]
+  uint64_t* pv_done = bars + 16;  // [2]
+  uint64_t* mma_done = bars + 18;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + F_BAR + F_NBAR * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + F_BAR + F_NBAR * 8 + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_t = p.n_t;
-  const int bh = blockIdx.x / n_t;
-  const int qt = n_t - 1 - (int)(blockIdx.x % n_t);  // longest rows first
+  const int n_pair = (p.n_t + 1) >> 1;
+  const int bh = blockIdx.x / n_pair;
+  const int qa = 2 * (n_pair - 1 - (int)(blockIdx.x % n_pair));  // longest rows first
+  const bool has_b = qa + 1 < p.n_t;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvz = b * p.Hkv + h / p.G;
-  const int n = qt + 1;  // key tiles at or below the diagonal
+  const int na = qa + 1;              // key tiles of tile a: 0 .. qa
+  const int nb = has_b ? qa + 2 : 0;  // key tiles of tile b: 0 .. qa + 1
+  const int n = has_b ? nb : na;
   constexpr uint32_t IDESC = tc::idesc_f16(AbFormat<T>::v, 128, 128, 0, 0);
   constexpr uint32_t IDESC_PV = tc::idesc_f16(AbFormat<T>::v, 128, 128, 0, 1);
+  // ring position of key tile j and of value tile j
+  auto u_k = [&](int j) { return WITH_O ? (j == 0 ? 0 : 2 * j - 1) : j; };
+  auto u_v = [&](int j) { return j == n - 1 ? 2 * n - 1 : 2 * j + 2; };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < FWD_KS; ++i) {
-      mbar_init(k_full + i, 1);
-      mbar_init(k_empty + i, 1);
+    for (int i = 0; i < FWD_RS; ++i) {
+      mbar_init(r_full + i, 1);
+      mbar_init(r_empty + i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(v_full + i, 1);
-      mbar_init(v_empty + i, 1);
-      mbar_init(s_full + i, 1);
-      mbar_init(s_free + i, 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, 128);
+      mbar_init(pv_done + x, 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
-    mbar_init(mma_done, 1);
+    mbar_init(s_free, 128);
+    mbar_init(mma_done, WITH_O ? 2 : 1);  // one commit per issuing thread
     *abort = 0;
     fence_barrier_init();
   }
@@ -161,96 +169,108 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
-  const uint32_t tmem = *tmem_slot;  // S0: +0, S1: +128, O: +256
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- TMA producers: lane 0 streams Q and the K tiles, lane 1 the V tiles ----
+    // ---- TMA producer: Q_a, Q_b, then K0 K1 V0 K2 V1 ... through the ring ---
     if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, has_b ? 2 * TILE : TILE);
+      for (int x = 0; x < (has_b ? 2 : 1); ++x) {
+        tc::tma_load_3d(smem + F_Q + x * TILE, &tq, 0, (qa + x) * SB, bh, q_full);
+        tc::tma_load_3d(smem + F_Q + x * TILE + SUB, &tq, 64, (qa + x) * SB, bh, q_full);
+      }
+      const int n_loads = n * LPS;
       int issued = 0;
-      mbar_arrive_expect_tx(q_full, TILE);
-      tc::tma_load_3d(smem + F_Q, &tq, 0, qt * SB, bh, q_full);
-      tc::tma_load_3d(smem + F_Q + SUB, &tq, 64, qt * SB, bh, q_full);
-      for (int j = 0; j < n; ++j) {
-        const int st = j % FWD_KS;
-        if (j >= FWD_KS && !one_wait(k_empty + st, ((j / FWD_KS) - 1) & 1, p.status, abort)) break;
-        mbar_arrive_expect_tx(k_full + st, TILE);
-        tc::tma_load_3d(smem + F_K + st * TILE, &tk, 0, j * SB, kvz, k_full + st);
-        tc::tma_load_3d(smem + F_K + st * TILE + SUB, &tk, 64, j * SB, kvz, k_full + st);
-        issued = j + 1;
+      for (int u = 0; u < n_loads; ++u) {
+        const int st = u % FWD_RS;
+        if (u >= FWD_RS && !one_wait(r_empty + st, ((u / FWD_RS) - 1) & 1, p.status, abort)) break;
+        // inverse of u_k / u_v
+        const bool is_v = WITH_O && u > 0 && (u == n_loads - 1 || (u & 1) == 0);
+        const int j = !WITH_O ? u : is_v ? (u == n_loads - 1 ? n - 1 : u / 2 - 1) : (u + 1) / 2;
+        const CUtensorMap* m = is_v ? &tv : &tk;
+        mbar_arrive_expect_tx(r_full + st, TILE);
+        tc::tma_load_3d(smem + F_R + st * TILE, m, 0, j * SB, kvz, r_full + st);
+        tc::tma_load_3d(smem + F_R + st * TILE + SUB, m, 64, j * SB, kvz, r_full + st);
+        issued = u + 1;
       }
       // drain: every issued load has landed before the CTA may exit
       mbar_wait_bounded(q_full, 0, p.status, 200000000ull);
-      for (int j = issued - FWD_KS < 0 ? 0 : issued - FWD_KS; j < issued; ++j)
-        mbar_wait_bounded(k_full + j % FWD_KS, (j / FWD_KS) & 1, p.status, 200000000ull);
-    } else if (lane == 1 && WITH_O) {
-      int issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int st = j % FWD_VS;
-        if (j >= FWD_VS && !one_wait(v_empty + st, ((j / FWD_VS) - 1) & 1, p.status, abort)) break;
-        mbar_arrive_expect_tx(v_full + st, TILE);
-        tc::tma_load_3d(smem + F_V + st * TILE, &tv, 0, j * SB, kvz, v_full + st);
-        tc::tma_load_3d(smem + F_V + st * TILE + SUB, &tv, 64, j * SB, kvz, v_full + st);
-        issued = j + 1;
-      }
-      for (int j = issued - FWD_VS < 0 ? 0 : issued - FWD_VS; j < issued; ++j)
-        mbar_wait_bounded(v_full + j % FWD_VS, (j / FWD_VS) & 1, p.status, 200000000ull);
+      for (int u = issued - FWD_RS < 0 ? 0 : issued - FWD_RS; u < issued; ++u)
+        mbar_wait_bounded(r_full + u % FWD_RS, (u / FWD_RS) & 1, p.status, 200000000ull);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer -----------------------------------------------------------
+    // ---- Q K^T issuer: S_a(j), S_b(j) in turn through the one S buffer --------
     if (lane == 0) {
-      const uint32_t sq = sbase + F_Q, sp = sbase + F_P;
-      auto issue_pv = [&](int t) -> bool {
-        if (!one_wait(p_full, t & 1, p.status, abort)) return false;
-        if (!one_wait(v_full + t % FWD_VS, (t / FWD_VS) & 1, p.status, abort)) return false;
+      const uint32_t sq = sbase + F_Q;
+      int n_s = 0;  // score tiles issued into the S buffer so far
+      auto issue_s = [&](int x, int j) -> bool {
+        if (n_s >= 1 && !one_wait(s_free, (n_s - 1) & 1, p.status, abort)) return false;
         tc::fence_after();
-        const uint32_t sv = sbase + F_V + (t % FWD_VS) * TILE;
+        const uint32_t sk = sbase + F_R + (u_k(j) % FWD_RS) * TILE;
 #pragma unroll
-        for (int kk = 0; kk < SB / 16; ++kk)
-          tc::mma_ss(tmem + 256, kdesc(sp, kk), mndesc(sv, kk), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
-        tc::commit(pv_done);
-        tc::commit(v_empty + t % FWD_VS);
+        for (int kk = 0; kk < SD / 16; ++kk)
+          tc::mma_ss(tmem, kdesc(sq + x * TILE, kk), kdesc(sk, kk), IDESC, kk > 0 ? 1u : 0u);
+        tc::commit(s_full + x);
+        ++n_s;
         return true;
       };
       bool ok = one_wait(q_full, 0, p.status, abort);
       for (int j = 0; ok && j < n; ++j) {
-        const int st = j % FWD_KS, sb = j & 1;
-        if (!one_wait(k_full + st, (j / FWD_KS) & 1, p.status, abort)) break;
-        if (j >= 2 && !one_wait(s_free + sb, ((j - 2) >> 1) & 1, p.status, abort)) break;
-        tc::fence_after();
-        const uint32_t sk = sbase + F_K + st * TILE;
-#pragma unroll
-        for (int kk = 0; kk < SD / 16; ++kk)
-          tc::mma_ss(tmem + sb * 128, kdesc(sq, kk), kdesc(sk, kk), IDESC, kk > 0 ? 1u : 0u);
-        tc::commit(s_full + sb);
-        tc::commit(k_empty + st);
-        if (WITH_O && j >= 1) ok = issue_pv(j - 1);
+        const int u = u_k(j);
+        if (!(ok = one_wait(r_full + u % FWD_RS, (u / FWD_RS) & 1, p.status, abort))) break;
+        if (j < na && !(ok = issue_s(0, j))) break;
+        if (j < nb && !(ok = issue_s(1, j))) break;
+        tc::commit(r_empty + u % FWD_RS);
       }
-      if (WITH_O && ok && !*abort) issue_pv(n - 1);
+      tc::commit(mma_done);
+      mbar_wait_bounded(mma_done, 0, p.status);
+    }
+  } else if (warp == FWD_THREADS / 32 - 1) {
+    // ---- P V issuer: O_a += P_a V(j), O_b += P_b V(j), P read from TMEM -------
+    if (lane == 0 && WITH_O) {
+      bool ok = true;
+      for (int j = 0; ok && j < n; ++j) {
+        const int u = u_v(j);
+        if (!(ok = one_wait(r_full + u % FWD_RS, (u / FWD_RS) & 1, p.status, abort))) break;
+        const uint32_t sv = sbase + F_R + (u % FWD_RS) * TILE;
+        for (int x = 0; x < 2; ++x) {
+          if (j >= (x ? nb : na)) continue;
+          if (!(ok = one_wait(p_full + x, j & 1, p.status, abort))) break;
+          tc::fence_after();
+#pragma unroll
+          for (int kk = 0; kk < SB / 16; ++kk)
+            tc::mma_ts(tmem + 256 + x * 128, tmem + 128 + x * 64 + kk * 8, mndesc(sv, kk), IDESC_PV,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          tc::commit(pv_done + x);
+        }
+        if (ok) tc::commit(r_empty + u % FWD_RS);
+      }
       tc::commit(mma_done);
       mbar_wait_bounded(mma_done, 0, p.status);
     }
   } else {
-    // ---- softmax warps: thread = query row ------------------------------------
+    // ---- softmax warpgroups: x = 0 (warps 2-5) tile a, x = 1 (warps 6-9) tile b;
+    //      thread = query row --------------------------------------------------
+    const int x = warp >= 6 ? 1 : 0;
+    const int nx = x ? nb : na;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    unsigned char* ps = smem + F_P;
+    const uint32_t ts = tmem + lane_off, tp = tmem + lane_off + 128 + x * 64;
+    const uint32_t to = tmem + lane_off + 256 + x * 128;
     float m_used = -INFINITY, l = 0.f;
     float s[SB];
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      const int sb = j & 1;
-      if (!(ok = warp_wait(s_full + sb, (j >> 1) & 1, p.status, abort))) break;
+    for (int j = 0; j < nx; ++j) {
+      if (!(ok = warp_wait(s_full + x, j & 1, p.status, abort))) break;
       tc::fence_after();
 #pragma unroll
-      for (int c = 0; c < SB; c += 32) tc::tmem_ld32(tmem + lane_off + sb * 128 + c, s + c);
+      for (int c = 0; c < SB; c += 32) tc::tmem_ld32(ts + c, s + c);
       tc::tmem_wait_ld();
       tc::fence_before();
-      tc::mbar_arrive(s_free + sb);
+      tc::mbar_arrive(s_free);
 
-      // raw row maximum with eight independent chains (the scale is positive,
-      // so scaling the maximum equals the maximum of the scaled scores)
-      if (j == n - 1) {  // diagonal tile: key c is visible to row r iff c <= r
+      if (j == nx - 1) {  // diagonal tile: key c is visible to row r iff c <= r
 #pragma unroll
         for (int c = 0; c < SB; ++c) s[c] = c <= r ? s[c] : -INFINITY;
       }
@@ -265,48 +285,48 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       const float alpha = m_new == m_used ? 1.f : tc::ex2(m_used - m_new);
       float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < SB; ++c) {
-        s[c] = tc::ex2(fmaf(s[c], p.sl2, -m_new));
-        r4[c & 3] += s[c];
+      for (int c0 = 0; c0 < SB; c0 += 16) {
+        float pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float e0 = tc::ex2(fmaf(s[c0 + 2 * i], p.sl2, -m_new));
+          const float e1 = tc::ex2(fmaf(s[c0 + 2 * i + 1], p.sl2, -m_new));
+          r4[(2 * i) & 3] += e0;
+          r4[(2 * i + 1) & 3] += e1;
+          if (WITH_O) pk[i] = __uint_as_float(pack2(e0, e1, (T*)nullptr));
+        }
+        if (WITH_O) {
+          if (c0 == 0 && j >= 1) {
+            if (!(ok = warp_wait(pv_done + x, (j - 1) & 1, p.status, abort))) break;
+            tc::fence_after();
+          }
+          tc::tmem_st8(tp + c0 / 2, pk);
+        }
       }
+      if (!ok) break;
       l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
       if (WITH_O) {
-        // P buffer and O are free once the previous P . V has completed
-        if (j >= 1) {
-          if (!(ok = warp_wait(pv_done, (j - 1) & 1, p.status, abort))) break;
-          tc::fence_after();
-          if (__any_sync(0xffffffffu, m_new != m_used)) {
-            const float a = m_new != m_used ? alpha : 1.f;
+        if (j >= 1 && __any_sync(0xffffffffu, m_new != m_used)) {
+          const float a = m_new != m_used ? alpha : 1.f;
 #pragma unroll 1
-            for (int c = 0; c < SD; c += 32) {
-              float o[32];
-              tc::tmem_ld32(tmem + lane_off + 256 + c, o);
-              tc::tmem_wait_ld();
+          for (int c = 0; c < SD; c += 16) {
+            float o[16];
+            tc::tmem_ld16(to + c, o);
+            tc::tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= a;
-              tc::tmem_st32(tmem + lane_off + 256 + c, o);
-            }
-            tc::tmem_wait_st();
+            for (int i = 0; i < 16; ++i) o[i] *= a;
+            tc::tmem_st16(to + c, o);
           }
         }
-#pragma unroll
-        for (int q = 0; q < SB / 8; ++q) {
-          uint4 w;
-          w.x = pack2(s[8 * q + 0], s[8 * q + 1], (T*)nullptr);
-          w.y = pack2(s[8 * q + 2], s[8 * q + 3], (T*)nullptr);
-          w.z = pack2(s[8 * q + 4], s[8 * q + 5], (T*)nullptr);
-          w.w = pack2(s[8 * q + 6], s[8 * q + 7], (T*)nullptr);
-          *reinterpret_cast<uint4*>(ps + sw_chunk(r, q)) = w;
-        }
-        fence_proxy_async_smem();
+        tc::tmem_wait_st();
         tc::fence_before();
-        tc::mbar_arrive(p_full);
+        tc::mbar_arrive(p_full + x);
       }
       m_used = m_new;
     }
-    const int row = qt * SB + r;
-    if (ok && WITH_O) ok = warp_wait(pv_done, (n - 1) & 1, p.status, abort);
-    if (ok) {
+    const int row = (qa + x) * SB + r;
+    if (nx > 0 && ok && WITH_O) ok = warp_wait(pv_done + x, (nx - 1) & 1, p.status, abort);
+    if (nx > 0 && ok) {
       tc::fence_after();
       if (row < p.T) p.lse[(size_t)bh * p.T + row] = (m_used + log2f(l)) * LN2;
       if (WITH_O) {
@@ -315,7 +335,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < SD; c += 32) {
           float o[32];
-          tc::tmem_ld32(tmem + lane_off + 256 + c, o);
+          tc::tmem_ld32(to + c, o);
           tc::tmem_wait_ld();
           if (row < p.T) {
 #pragma unroll
@@ -339,7 +359,6 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     tc::tmem_dealloc(tmem, 512);
   }
 }
-
 // ------------------------------------------------------------------------------
 // 2. column sums: received mass per key, per query head
 // ------------------------------------------------------------------------------
@@ -602,12 +621,13 @@ int launch_summary(const ic_summary_args* a, cudaStream_t st) {
 
   static int lim_fwd_o = 0, lim_fwd = 0, lim_col = 0;
   const unsigned grid = (unsigned)(BHq * n_t);
+  const unsigned grid_fwd = (unsigned)(BHq * ((n_t + 1) / 2));
   if (a->out) {
     if ((rc = ensure_dynamic_smem(summary_fwd_kernel<T, true>, F_BYTES, &lim_fwd_o)) != IC_OK) return rc;
-    summary_fwd_kernel<T, true><<<grid, FWD_THREADS, F_BYTES, st>>>(mq, mk, mv, p);
+    summary_fwd_kernel<T, true><<<grid_fwd, FWD_THREADS, F_BYTES, st>>>(mq, mk, mv, p);
   } else {
     if ((rc = ensure_dynamic_smem(summary_fwd_kernel<T, false>, F_BYTES, &lim_fwd)) != IC_OK) return rc;
-    summary_fwd_kernel<T, false><<<grid, FWD_THREADS, F_BYTES, st>>>(mq, mk, mv, p);
+    summary_fwd_kernel<T, false><<<grid_fwd, FWD_THREADS, F_BYTES, st>>>(mq, mk, mv, p);
   }
   if ((rc = launch_status("summary_fwd_kernel")) != IC_OK) return rc;
   if (!a->head_mass) return IC_OK;
