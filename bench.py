@@ -225,7 +225,7 @@ def summary_leg(device, iters=10, batch=None):
     tflops = flops / (ms / 1e3) / 1e12
     del q, k, v
     return {"workload": f"summary pass: {B} sequences x {Hq}/{Hkv} heads x {T} tokens causal, head_dim {D}, bf16",
-            "kernels": "summary_fwd_kernel + summary_colsum_kernel + summary_reduce_kernel (ic_summary_score)",
+            "kernels": "summary_fwd_kernel + summary_colsum_kernel + summary_head_sum_kernel + summary_normalise_kernel (ic_summary_score)",
             "ms_per_call": ms, "alg_tflop_per_call": flops / 1e12,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": tflops / peak, "peak_kind": f"{kind} (MEASURED_PEAKS.json bf16_tflops, burst)"}}

@@ -16,8 +16,9 @@
 //     diagonal, then p = exp2(s * scale * log2 e - lse2) with one thread per
 //     key summing its column in fp32 registers — a fixed order, so the result
 //     is deterministic.
-//  3. summary_reduce_kernel: colsum = sum over heads in head order, and the
-//     normalised importance with a fixed-shape block reduction.
+//  3. summary_head_sum_kernel: colsum = sum over heads in head order; then
+//     summary_normalise_kernel: the normalised importance with a fixed-shape
+//     block reduction.
 //
 // Roles inside a CTA: warp 0 issues TMA loads, warp 1 owns TMEM and issues
 // the MMAs (one thread; the forward kernel hands P V to a second issuing
@@ -522,23 +523,31 @@ __global__ void __launch_bounds__(COL_THREADS, 1)
 // 3. colsum over heads and the normalised importance (one CTA per sequence)
 // ------------------------------------------------------------------------------
 constexpr int RED_THREADS = 1024;
+constexpr int RED_COLS = 1024;  // columns per CTA of the head sum
 
+// colsum[b, j] (+)= sum over heads in head order of head_mass[b, h, j]; one
+// CTA per (sequence, 1024 columns).
+__global__ void __launch_bounds__(RED_COLS)
+    summary_head_sum_kernel(const float* __restrict__ head_mass, float* colsum, int Hq, int T, int accumulate) {
+  const int b = blockIdx.y, j = blockIdx.x * RED_COLS + threadIdx.x;
+  if (j >= T) return;
+  const float* hm = head_mass + (size_t)b * Hq * T + j;
+  float* cs = colsum + (size_t)b * T + j;
+  float v = accumulate ? *cs : 0.f;
+  for (int hh = 0; hh < Hq; ++hh) v += hm[(size_t)hh * T];
+  *cs = v;
+}
+
+// importance[b, :] = colsum[b, :] / sum(colsum[b, :]), the sum taken by a
+// fixed-shape block reduction (one CTA per sequence).
 __global__ void __launch_bounds__(RED_THREADS)
-    summary_reduce_kernel(const float* __restrict__ head_mass, float* colsum, float* importance, int Hq, int T,
-                          int accumulate) {
+    summary_normalise_kernel(const float* __restrict__ colsum, float* importance, int T) {
   __shared__ float part[RED_THREADS / 32];
   __shared__ float total_s;
   const int b = blockIdx.x;
-  const float* hm = head_mass + (size_t)b * Hq * T;
-  float* cs = colsum + (size_t)b * T;
+  const float* cs = colsum + (size_t)b * T;
   float tot = 0.f;
-  for (int j = threadIdx.x; j < T; j += RED_THREADS) {
-    float v = accumulate ? cs[j] : 0.f;
-    for (int hh = 0; hh < Hq; ++hh) v += hm[(size_t)hh * T + j];
-    cs[j] = v;
-    tot += v;
-  }
-  if (!importance) return;
+  for (int j = threadIdx.x; j < T; j += RED_THREADS) tot += cs[j];
   tot = warp_sum(tot);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = tot;
   __syncthreads();
@@ -634,9 +643,12 @@ int launch_summary(const ic_summary_args* a, cudaStream_t st) {
   if ((rc = ensure_dynamic_smem(summary_colsum_kernel<T>, C_BYTES, &lim_col)) != IC_OK) return rc;
   summary_colsum_kernel<T><<<grid, COL_THREADS, C_BYTES, st>>>(mq, mk, p);
   if ((rc = launch_status("summary_colsum_kernel")) != IC_OK) return rc;
-  summary_reduce_kernel<<<a->batch, RED_THREADS, 0, st>>>(a->head_mass, a->colsum, a->importance,
-                                                          a->num_q_heads, T_, a->accumulate);
-  return launch_status("summary_reduce_kernel");
+  summary_head_sum_kernel<<<dim3((unsigned)((T_ + RED_COLS - 1) / RED_COLS), (unsigned)a->batch), RED_COLS, 0, st>>>(
+      a->head_mass, a->colsum, a->num_q_heads, T_, a->accumulate);
+  if ((rc = launch_status("summary_head_sum_kernel")) != IC_OK) return rc;
+  if (!a->importance) return IC_OK;
+  summary_normalise_kernel<<<a->batch, RED_THREADS, 0, st>>>(a->colsum, a->importance, T_);
+  return launch_status("summary_normalise_kernel");
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
