@@ -433,6 +433,14 @@ typedef struct ic_compact_attn_args {
 } ic_compact_attn_args;
 int ic_compact_attention(const ic_compact_attn_args* a, void* stream);
 
+/* ---- mapped host buffers ------------------------------------------------------
+ * The device address of page-locked host memory (cudaHostGetDevicePointer),
+ * so a decode step can read q / k_new / v_new from, and write `out` to, the
+ * caller's pinned host buffers directly over PCIe, with no staging copies.
+ * No reference counterpart (the reference moves tensors with .to(device)).
+ * IC_ERR_INVALID_ARG when `host` is not page-locked mapped memory. */
+int ic_host_device_pointer(const void* host, void** device);
+
 /* ---- library information --------------------------------------------------*/
 const char* ic_status_str(int status);
 int ic_abi_version(void);

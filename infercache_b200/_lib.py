@@ -189,6 +189,7 @@ ENTRY_POINTS = {
     "ic_compact_attention": ic_compact_attn_args,
 }
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
+HOST_ENTRY_POINTS = ["ic_host_device_pointer"]
 
 _LIB = None
 
@@ -214,6 +215,8 @@ def load(path: Path = LIB_PATH):
     lib.ic_device_check.restype = c_int
     lib.ic_last_error.argtypes = []
     lib.ic_last_error.restype = c_char_p
+    lib.ic_host_device_pointer.argtypes = [c_void_p, POINTER(c_void_p)]
+    lib.ic_host_device_pointer.restype = c_int
     _LIB = lib
     return lib
 
@@ -253,6 +256,17 @@ def require_device(device: torch.device) -> None:
         rc = lib.ic_device_check()
     raise_for(rc, "device check")
     _DEVICE_OK[idx] = True
+
+
+def host_device_pointer(t: torch.Tensor) -> int:
+    """Device address of a pinned (page-locked, mapped) host tensor's data
+    (``ic_host_device_pointer``), for kernels that read or write it over PCIe."""
+    if t.device.type != "cpu" or not t.is_pinned():
+        raise ValueError("host_device_pointer needs a pinned host tensor")
+    lib = load()
+    out = c_void_p()
+    raise_for(lib.ic_host_device_pointer(c_void_p(t.data_ptr()), ctypes.byref(out)), "ic_host_device_pointer")
+    return int(out.value)
 
 
 def ptr(t) -> int:

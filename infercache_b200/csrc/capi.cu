@@ -41,6 +41,18 @@ extern "C" const char* ic_status_str(int status) {
 
 extern "C" int ic_abi_version(void) { return IC_ABI_VERSION; }
 
+extern "C" int ic_host_device_pointer(const void* host, void** device) {
+  if (!host || !device) return IC_ERR_INVALID_ARG;
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, const_cast<void*>(host), 0) != cudaSuccess) {
+    cudaGetLastError();
+    ic::set_last_error("ic_host_device_pointer: not page-locked mapped host memory");
+    return IC_ERR_INVALID_ARG;
+  }
+  *device = d;
+  return IC_OK;
+}
+
 extern "C" int ic_device_check(void) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {

@@ -36,6 +36,8 @@
 
 namespace ic {
 namespace {
+__device__ __forceinline__ unsigned short u16_bits(__half x) { return __half_as_ushort(x); }
+__device__ __forceinline__ unsigned short u16_bits(__nv_bfloat16 x) { return __bfloat16_as_ushort(x); }
 
 constexpr int LN_D = 128;
 constexpr int LN_R = 16;                       // rows per chunk
@@ -367,16 +369,28 @@ __global__ void __launch_bounds__(W * 32, 8 / W) decode_lean_kernel(const ic_dec
         stat[HS + head] = inv;
       }
       if (head < G) {
+        // eight consecutive outputs leave as one 16-byte store (two for fp32),
+        // which also keeps the writes whole when `out` is mapped host memory
+        float x[8];
 #pragma unroll
-        for (int d = d0; d < d0 + 8; ++d) {
-          float x = 0.f;
+        for (int i = 0; i < 8; ++i) {
+          x[i] = 0.f;
 #pragma unroll
-          for (int w = 0; w < W; ++w) x = fmaf(wo[(w * HS + head) * LN_D + d], f[w], x);
-          x *= inv;
-          if (a.out_dtype == IC_F32)
-            static_cast<float*>(a.out)[ob + static_cast<size_t>(head) * LN_D + d] = x;
-          else
-            static_cast<T*>(a.out)[ob + static_cast<size_t>(head) * LN_D + d] = DT<T>::from_f(x);
+          for (int w = 0; w < W; ++w) x[i] = fmaf(wo[(w * HS + head) * LN_D + d0 + i], f[w], x[i]);
+          x[i] *= inv;
+        }
+        const size_t o0 = ob + static_cast<size_t>(head) * LN_D + d0;
+        if (a.out_dtype == IC_F32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + o0);
+          dst[0] = make_float4(x[0], x[1], x[2], x[3]);
+          dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+        } else {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            w[i] = static_cast<uint32_t>(u16_bits(DT<T>::from_f(x[2 * i]))) |
+                   (static_cast<uint32_t>(u16_bits(DT<T>::from_f(x[2 * i + 1]))) << 16);
+          *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + o0) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }

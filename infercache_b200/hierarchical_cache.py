@@ -262,11 +262,31 @@ class SessionBatch:
         self._keep = pos
         return out
 
+    def _step_raw(self, q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, num_q_heads: int,
+                  out_dtype: torch.dtype, pos: torch.Tensor) -> None:
+        """``step`` on raw device addresses of contiguous [L, S, H, D] buffers
+        in the cache dtype (e.g. mapped pinned host memory); no checks."""
+        cfg = self.cfg
+        S, D = self.num_sessions, cfg.head_dim
+        st = self._step
+        d = st.layer0
+        self._prepare_decode(d, num_q_heads)
+        d.q, d.k_new, d.v_new, d.out = q_ptr, k_ptr, v_ptr, out_ptr
+        d.out_dtype = _lib.dtype_code(out_dtype)
+        st.evict.pdl = 1 if self.pdl else 0
+        st.q_layer_stride = S * num_q_heads * D
+        st.kv_layer_stride = S * cfg.num_kv_heads * D
+        st.out_layer_stride = S * num_q_heads * D
+        st.evict.new_pos = pos.data_ptr()
+        st.evict.decay = cfg.decay
+        _lib.call("ic_decode_step", st)
+        self._keep = pos
+
     def host_stepper(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
-                     out_host, positions: torch.Tensor) -> "HostStepper":
+                     out_host, positions: torch.Tensor, zero_copy: bool = False) -> "HostStepper":
         """A decode step from pinned host buffers, captured once as a CUDA graph
         (see ``HostStepper``)."""
-        return HostStepper(self, q_host, k_host, v_host, out_host, positions)
+        return HostStepper(self, q_host, k_host, v_host, out_host, positions, zero_copy=zero_copy)
 
     def _positions_arg(self, positions) -> torch.Tensor:
         if isinstance(positions, torch.Tensor) and positions.device == self.device and positions.dtype == torch.int64:
@@ -468,12 +488,20 @@ class HostStepper:
 
     ``out_host`` is one tensor, or a pair for a pipelined stepper: the copy of
     step i's output to ``out_host[i % 2]`` then runs on a copy stream while
-    step i + 1 computes (a step's inputs are still copied before it starts).
-    ``run()`` returns the index of the buffer receiving this step's output;
-    ``wait(index)`` (or ``synchronize()``) makes it readable."""
+    step i + 1 computes.  ``run()`` returns the index of the buffer receiving
+    this step's output; ``wait(index)`` (or ``synchronize()``) makes it
+    readable.
+
+    ``zero_copy`` makes the decode kernels read q / k / v from, and write the
+    output to, the pinned host buffers themselves (mapped host memory over
+    PCIe): no staging copies and no copy launches, at the price of PCIe
+    latency inside every layer's kernel.  (Measured at 16 sessions x 36
+    layers: 0.250 ms per step against 0.222 ms staged.  Copies on a second
+    stream do not overlap the step either: run beside the decode kernels, a
+    2.36 MB upload took 176 us instead of 51 us and slowed the step by 93 us.)"""
 
     def __init__(self, batch: "SessionBatch", q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
-                 out_host, positions: torch.Tensor):
+                 out_host, positions: torch.Tensor, zero_copy: bool = False):
         outs = tuple(out_host) if isinstance(out_host, (tuple, list)) else (out_host,)
         if len(outs) not in (1, 2):
             raise ValueError("out_host must be a tensor or a pair of tensors")
@@ -487,7 +515,41 @@ class HostStepper:
         self.q_host, self.k_host, self.v_host, self.out_host = q_host, k_host, v_host, outs
         self.positions = positions
         self.pipelined = len(outs) == 2
+        self.zero_copy = bool(zero_copy)
         dev = batch.device
+        if self.zero_copy:
+            cfg = batch.cfg
+            L, S = cfg.num_layers, batch.num_sessions
+            Hq = q_host.shape[2] if q_host.dim() == 4 else -1
+            if (q_host.dim() != 4 or tuple(q_host.shape[:2]) != (L, S) or q_host.shape[3] != cfg.head_dim or
+                    tuple(k_host.shape) != (L, S, cfg.num_kv_heads, cfg.head_dim) or k_host.shape != v_host.shape):
+                raise ValueError("q_host [L, S, Hq, D], k_host / v_host [L, S, Hkv, D] expected")
+            for t in (q_host, k_host, v_host):
+                if t.dtype != cfg.dtype:
+                    raise ValueError("q_host / k_host / v_host must be in the cache dtype")
+            for o in outs:
+                if o.shape != q_host.shape:
+                    raise ValueError("out_host must be shaped like q_host")
+            self.h2d_bytes = sum(t.numel() * t.element_size() for t in (q_host, k_host, v_host))
+            self.d2h_bytes = outs[0].numel() * outs[0].element_size()
+            qd, kd, vd = (_lib.host_device_pointer(t) for t in (q_host, k_host, v_host))
+            ods = [_lib.host_device_pointer(o) for o in outs]
+            cap = torch.cuda.Stream(device=dev)
+            cap.wait_stream(torch.cuda.current_stream(dev))
+            self.graphs = []
+            for k in range(len(outs)):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=cap, capture_error_mode="relaxed"):
+                    batch._step_raw(qd, kd, vd, ods[k], Hq, outs[k].dtype, positions)
+                    positions.add_(1)
+                self.graphs.append(gr)
+            self.graph = self.graphs[0]
+            self._copy = None
+            self._computed = [torch.cuda.Event() for _ in outs]
+            self._copied = self._computed
+            self._used = [False] * len(outs)
+            self._next = 0
+            return
         self._q = torch.empty(q_host.shape, dtype=q_host.dtype, device=dev)
         self._k = torch.empty(k_host.shape, dtype=k_host.dtype, device=dev)
         self._v = torch.empty(v_host.shape, dtype=v_host.dtype, device=dev)
@@ -519,6 +581,15 @@ class HostStepper:
     def run(self, sync: bool = False) -> int:
         k = self._next
         main = torch.cuda.current_stream(self.batch.device)
+        if self.zero_copy:
+            self.graphs[k].replay()  # the kernels write out_host[k] themselves
+            self._computed[k].record(main)
+            self._used[k] = True
+            if self.pipelined:
+                self._next = 1 - k
+            if sync:
+                self.wait(k)
+            return k
         if self.pipelined and self._used[k]:
             main.wait_event(self._copied[k])  # the device output buffer has been read
         self.graphs[k].replay()
@@ -536,7 +607,7 @@ class HostStepper:
 
     def wait(self, index: int = 0) -> None:
         """Block the host until out_host[index] holds its step's output."""
-        if self.pipelined:
+        if self.pipelined or self.zero_copy:
             self._copied[index].synchronize()
         else:
             torch.cuda.current_stream(self.batch.device).synchronize()
@@ -545,7 +616,7 @@ class HostStepper:
         """Make `stream` (default: the current one) wait for every pending
         output copy, without blocking the host."""
         st = stream or torch.cuda.current_stream(self.batch.device)
-        if self.pipelined:
+        if self.pipelined or self.zero_copy:
             for k, used in enumerate(self._used):
                 if used:
                     st.wait_event(self._copied[k])

@@ -32,7 +32,7 @@ def test_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     # and the binding covers exactly the declared entry points
-    assert set(names) == set(_lib.ENTRY_POINTS) | set(_lib.INFO_ENTRY_POINTS)
+    assert set(names) == set(_lib.ENTRY_POINTS) | set(_lib.INFO_ENTRY_POINTS) | set(_lib.HOST_ENTRY_POINTS)
 
 
 def test_status_strings():
@@ -40,6 +40,14 @@ def test_status_strings():
     assert lib.ic_status_str(0) == b"ok"
     assert lib.ic_status_str(_lib.IC_ERR_OUT_OF_PAGES) == b"page pool exhausted"
     assert lib.ic_status_str(12345) == b"unknown status"
+
+
+def test_host_device_pointer_rejects_null_without_cuda_call():
+    lib = _lib.load()
+    import ctypes
+    assert lib.ic_host_device_pointer(None, None) == _lib.IC_ERR_INVALID_ARG
+    out = ctypes.c_void_p()
+    assert lib.ic_host_device_pointer(None, ctypes.byref(out)) == _lib.IC_ERR_INVALID_ARG
 
 
 def test_null_args_rejected_without_launch():

@@ -104,6 +104,33 @@ def test_pipelined_host_stepper_matches_eager_steps():
         assert torch.equal(getattr(a, key), getattr(b, key)), key
 
 
+def test_zero_copy_host_stepper_matches_eager_steps():
+    """The stepper whose kernels read and write the pinned host buffers
+    directly (zero_copy) gives the same outputs and cache state as eager
+    steps."""
+    a = _batch(3, seed=17)
+    b = _batch(3, seed=17)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    q = torch.randn(3, 3, 16, 128, generator=g, device="cuda").half()
+    k = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    v = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    pos = torch.full((3,), 900, dtype=torch.int64, device="cuda")
+    ohs = tuple(torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2))
+    st = b.host_stepper(q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory(), ohs, pos,
+                        zero_copy=True)
+    assert st.zero_copy
+    refs = [a.step(q, k, v, torch.full((3,), 900 + i, dtype=torch.int64, device="cuda")).cpu() for i in range(10)]
+    for i in range(10):
+        idx = st.run()
+        st.wait(idx)
+        assert torch.equal(ohs[idx], refs[i]), i
+    st.synchronize()
+    torch.cuda.synchronize()
+    for key in ("positions", "importance", "occupied", "ctrl", "counters"):
+        assert torch.equal(getattr(a, key), getattr(b, key)), key
+    b.check_device_status()
+
+
 def test_state_dict_round_trip_and_async_stats():
     """HierarchicalKVCache.state_dict / load_state_dict through host memory,
     and the asynchronous stats readback."""
