@@ -36,8 +36,6 @@
 
 namespace ic {
 namespace {
-__device__ __forceinline__ unsigned short u16_bits(__half x) { return __half_as_ushort(x); }
-__device__ __forceinline__ unsigned short u16_bits(__nv_bfloat16 x) { return __bfloat16_as_ushort(x); }
 
 constexpr int LN_D = 128;
 constexpr int LN_R = 16;                       // rows per chunk
@@ -385,12 +383,9 @@ __global__ void __launch_bounds__(W * 32, 8 / W) decode_lean_kernel(const ic_dec
           dst[0] = make_float4(x[0], x[1], x[2], x[3]);
           dst[1] = make_float4(x[4], x[5], x[6], x[7]);
         } else {
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            w[i] = static_cast<uint32_t>(u16_bits(DT<T>::from_f(x[2 * i]))) |
-                   (static_cast<uint32_t>(u16_bits(DT<T>::from_f(x[2 * i + 1]))) << 16);
-          *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + o0) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + o0) =
+              make_uint4(pack_pair<T>(x[0], x[1]), pack_pair<T>(x[2], x[3]), pack_pair<T>(x[4], x[5]),
+                         pack_pair<T>(x[6], x[7]));
         }
       }
     }
