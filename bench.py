@@ -553,7 +553,7 @@ def main():
                 "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": config_dict(spec, world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": traffic,
-                             "kernel": "decode_stream_kernel (ic_decode_step), one launch = 16 sessions x 1 layer",
+                             "kernel": "decode_lean_kernel (ic_decode_step), one launch = 16 sessions x 1 layer",
                              "alg_bytes_per_launch": alg_bytes, "launch_us": dec_launch_s * 1e6,
                              "launch_us_basis": "step time / 36 inside the step graph, eviction included",
                              "sequential_attend_us": seq_launch_s * 1e6,
