@@ -135,3 +135,35 @@ def paged_tokens(n, seed):
     k = torch.randn(sp["layers"], sp["heads"], n, sp["d"], generator=g)
     v = torch.randn(sp["layers"], sp["heads"], n, sp["d"], generator=g)
     return k, v
+
+
+# Graph (cluster-routed) cache.  Layer-0 / head-0 keys are drawn around a few
+# random directions so that tokens form clusters; the other heads and layers
+# are plain noise.  Positions are the token indices.
+GRAPH = {
+    "push": dict(L=3, H=2, D=128, n_clusters=4, cap=6, sink=4, recent=8, threshold=0.3, T=120, n_dirs=5,
+                 seed=31),
+    "load": dict(L=2, H=2, D=128, n_clusters=6, cap=5, sink=4, recent=16, threshold=0.3, T=200, n_dirs=4,
+                 seed=32),
+    "wide": dict(L=4, H=4, D=128, n_clusters=16, cap=32, sink=4, recent=128, threshold=0.3, T=1500, n_dirs=12,
+                 seed=34),
+}
+# retrieve() cases: (threshold or None, top_n or None)
+GRAPH_QUERIES = [(None, None), (0.6, None), (0.95, None), (None, 1), (None, 3)]
+
+
+def graph_inputs(name):
+    sp = GRAPH[name]
+    g = torch.Generator().manual_seed(sp["seed"])
+    L, H, D, T = sp["L"], sp["H"], sp["D"], sp["T"]
+    dirs = torch.randn(sp["n_dirs"], D, generator=g)
+    dirs = dirs / dirs.norm(dim=1, keepdim=True)
+    which = torch.randint(0, sp["n_dirs"], (T,), generator=g)
+    k = torch.randn(L, H, T, D, generator=g)
+    k[0, 0] = dirs[which] * 4.0 + torch.randn(T, D, generator=g) * 0.7
+    v = torch.randn(L, H, T, D, generator=g)
+    scores = torch.rand(T, generator=g)
+    nq = len(GRAPH_QUERIES)
+    qdir = torch.randint(0, sp["n_dirs"], (nq,), generator=g)
+    queries = dirs[qdir][:, None, :] * 3.0 + torch.randn(nq, H, D, generator=g) * 0.8
+    return k.half(), v.half(), scores, queries
