@@ -433,6 +433,61 @@ typedef struct ic_compact_attn_args {
 } ic_compact_attn_args;
 int ic_compact_attention(const ic_compact_attn_args* a, void* stream);
 
+/* ---- Graph (cluster-routed) cache: GraphKVCache (graph_cache.py:218-495) --
+ * One slot store K/V [L, H, NS, D], NS = sink + recent + n_clusters *
+ * cluster_capacity, slots ordered sinks, ring, cluster 0, cluster 1, ...;
+ * head_dim 128. */
+typedef struct ic_graph_state {
+  void* k;
+  void* v;
+  int64_t* positions;       /* [NS], -1 empty */
+  float* scores;            /* [n_clusters * cluster_capacity] */
+  float* centroid;          /* [n_clusters, head_dim] */
+  int32_t* cl_fill;         /* [n_clusters] */
+  int32_t* c_count;         /* [n_clusters] tokens in each centroid */
+  int32_t* ctrl;            /* [3]: sink fill, ring pointer, ring fill */
+  int32_t num_layers, num_kv_heads, head_dim, dtype;
+  int32_t sink_size, recent_size, n_clusters, cluster_capacity;
+  float sim_threshold;
+  int32_t _pad;
+} ic_graph_state;
+
+/* push (graph_cache.py:287-361) of T tokens in order, or, with reset, the
+ * bulk load_from_summary (:442-467) into a cleared cache.  k_src / v_src:
+ * the tokens' K/V in the cache dtype, element offsets l * stride_l +
+ * h * stride_h + t * stride_t, D contiguous, rows 16-byte aligned;
+ * positions int64 [T] and scores float [T] (scores may be NULL: 0) on the
+ * device; slot_src int32 [NS] scratch. */
+typedef struct ic_graph_push_args {
+  ic_graph_state g;
+  const void* k_src;
+  const void* v_src;
+  int64_t stride_l, stride_h, stride_t;
+  const int64_t* positions;
+  const float* scores;
+  int32_t* slot_src;
+  int32_t T;
+  int32_t reset;
+} ic_graph_push_args;
+int ic_graph_push(const ic_graph_push_args* a, void* stream);
+
+/* retrieve's cluster choice and token order (graph_cache.py:363-440): query
+ * float [H, head_dim]; top_n > 0 selects the top_n clusters by centroid
+ * similarity of the head-mean query, else those with similarity >= threshold
+ * (at least the best); selected uint8 [n_clusters]; slots int32 [NS] gets
+ * the retrieve order (sinks, ring by position, selected clusters by
+ * position) and *count its length. */
+typedef struct ic_graph_select_args {
+  ic_graph_state g;
+  const float* query;
+  float threshold;
+  int32_t top_n;
+  uint8_t* selected;
+  int32_t* slots;
+  int32_t* count;
+} ic_graph_select_args;
+int ic_graph_select(const ic_graph_select_args* a, void* stream);
+
 /* ---- mapped host buffers ------------------------------------------------------
  * The device address of page-locked host memory (cudaHostGetDevicePointer),
  * so a decode step can read q / k_new / v_new from, and write `out` to, the

@@ -10,6 +10,7 @@ Public API (the reference's names):
     TwoPassConfig, SummaryResult, TwoPassEngine        two_pass
     gather_cache_kv, scatter_importance, topk_min_slot,
     compact_sdp_attention, GPUImportanceTracker        cache_ops (the triton_ops names)
+    ClusterConfig, GraphKVCache, MultiClusterCache     graph_cache (cluster-routed L2)
 
 Importing the package needs no GPU; constructing a cache does.
 """
@@ -20,5 +21,6 @@ from .summary import SummaryScores, attention_mass, summary_score  # noqa: F401
 from .two_pass import SummaryResult, TwoPassConfig, TwoPassEngine  # noqa: F401
 from .cache_ops import (GPUImportanceTracker, compact_sdp_attention, gather_cache_kv,  # noqa: F401
                         scatter_importance, topk_min_slot)
+from .graph_cache import ClusterConfig, GraphKVCache, MultiClusterCache  # noqa: F401
 
 __version__ = "0.1.0"

@@ -88,6 +88,25 @@ class ic_evict_args(Structure):
                 ("new_pos", c_void_p), ("events", c_void_p)]
 
 
+class ic_graph_state(Structure):
+    _fields_ = [("k", c_void_p), ("v", c_void_p), ("positions", c_void_p), ("scores", c_void_p),
+                ("centroid", c_void_p), ("cl_fill", c_void_p), ("c_count", c_void_p), ("ctrl", c_void_p),
+                ("num_layers", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32), ("dtype", c_int32),
+                ("sink_size", c_int32), ("recent_size", c_int32), ("n_clusters", c_int32),
+                ("cluster_capacity", c_int32), ("sim_threshold", c_float), ("_pad", c_int32)]
+
+
+class ic_graph_push_args(Structure):
+    _fields_ = [("g", ic_graph_state), ("k_src", c_void_p), ("v_src", c_void_p), ("stride_l", c_int64),
+                ("stride_h", c_int64), ("stride_t", c_int64), ("positions", c_void_p), ("scores", c_void_p),
+                ("slot_src", c_void_p), ("T", c_int32), ("reset", c_int32)]
+
+
+class ic_graph_select_args(Structure):
+    _fields_ = [("g", ic_graph_state), ("query", c_void_p), ("threshold", c_float), ("top_n", c_int32),
+                ("selected", c_void_p), ("slots", c_void_p), ("count", c_void_p)]
+
+
 class ic_step_args(Structure):
     _fields_ = [("layer0", ic_decode_args), ("q_layer_stride", c_int64), ("kv_layer_stride", c_int64),
                 ("out_layer_stride", c_int64), ("evict", ic_evict_args)]
@@ -187,6 +206,8 @@ ENTRY_POINTS = {
     "ic_scatter_mass": ic_scatter_mass_args,
     "ic_argmin_range": ic_argmin_args,
     "ic_compact_attention": ic_compact_attn_args,
+    "ic_graph_push": ic_graph_push_args,
+    "ic_graph_select": ic_graph_select_args,
 }
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
 HOST_ENTRY_POINTS = ["ic_host_device_pointer"]
