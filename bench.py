@@ -290,6 +290,88 @@ def paged_leg(device, iters=5):
                          "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
 
 
+GRAPH_WORKLOAD = dict(layers=36, heads=2, d=128, n_clusters=16, cap=32, sink=4, recent=128, threshold=0.3,
+                      prompt=2048, pushes=256, n_dirs=12, seed=5)
+
+
+def graph_leg(device, iters=5, cpu_sample=0):
+    """Graph (cluster-routed) cache, Qwen2.5-3B-shaped (36 layers, 2 KV heads,
+    head_dim 128, fp16), 16 clusters x 32 + 4 sinks + 128 recent:
+    load_from_summary of a 2048-token prompt (one routing launch over the
+    prompt's layer-0 / head-0 keys, then one parallel copy of the K/V rows
+    that stay), 256 single-token pushes, and retrieve() with the default
+    threshold.  Keys of layer 0 / head 0 are drawn around 12 directions so the
+    tokens form clusters.  With cpu_sample > 0 the oracle's restatement of the
+    reference's load times that many tokens on the host for comparison."""
+    from infercache_b200 import ClusterConfig, GraphKVCache
+    w = GRAPH_WORKLOAD
+    L, H, D, T = w["layers"], w["heads"], w["d"], w["prompt"]
+    g = torch.Generator(device=device).manual_seed(w["seed"])
+    dirs = torch.randn(w["n_dirs"], D, generator=g, device=device)
+    dirs = dirs / dirs.norm(dim=1, keepdim=True)
+    which = torch.randint(0, w["n_dirs"], (T + w["pushes"],), generator=g, device=device)
+    k = torch.randn(L, H, T + w["pushes"], D, generator=g, device=device)
+    k[0, 0] = dirs[which] * 4.0 + torch.randn(T + w["pushes"], D, generator=g, device=device) * 0.7
+    k = k.half()
+    v = torch.randn(L, H, T + w["pushes"], D, generator=g, device=device).half()
+    scores = torch.rand(T + w["pushes"], generator=g, device=device)
+    cfg = ClusterConfig(num_layers=L, num_kv_heads=H, head_dim=D, n_clusters=w["n_clusters"],
+                        cluster_capacity=w["cap"], sim_threshold=w["threshold"], sink_size=w["sink"],
+                        recent_size=w["recent"], dtype=torch.float16)
+    c = GraphKVCache(cfg, device)
+    pkv = tuple((k[li][None, :, :T], v[li][None, :, :T]) for li in range(L))
+    c.load_from_summary(pkv, scores[:T])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        c.load_from_summary(pkv, scores[:T])
+    e1.record()
+    torch.cuda.synchronize()
+    load_ms = e0.elapsed_time(e1) / iters
+    occupied = int((c.positions >= 0).sum())
+    moved = occupied * L * H * D * 2 * 2 * 2  # K + V rows kept, fp16, read + write
+    kt = [k[:, :, t:t + 1] for t in range(T, T + w["pushes"])]
+    vt = [v[:, :, t:t + 1] for t in range(T, T + w["pushes"])]
+    e0.record()
+    for i in range(w["pushes"]):
+        c.push(kt[i], vt[i], T + i, float(i % 7) / 7.0)
+    e1.record()
+    torch.cuda.synchronize()
+    push_us = e0.elapsed_time(e1) * 1e3 / w["pushes"]
+    q = k[:, :, T - 1][0].float()
+    c.retrieve(q)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        pk, sel = c.retrieve(q)
+    retrieve_us = (time.perf_counter() - t0) * 1e6 / iters
+    out = {"workload": f"graph cache: {L} layers x {H} KV heads x {D}, fp16, {w['n_clusters']} clusters x "
+                       f"{w['cap']} + {w['sink']} sinks + {w['recent']} recent; load_from_summary of a {T}-token "
+                       f"prompt, {w['pushes']} single pushes, retrieve at threshold {w['threshold']}",
+           "kernels": "graph_route_kernel + graph_copy_kernel (ic_graph_push); graph_select_kernel "
+                      "(ic_graph_select) + index_rows_kernel for K and for V (retrieve)",
+           "load_ms": load_ms, "load_tokens_per_s": T / (load_ms / 1e3), "push_us": push_us,
+           "retrieve_us_host_clock": retrieve_us, "retrieved_tokens": int(pk[0][0].shape[2]) if pk else 0,
+           "clusters_selected": int(sel.sum()),
+           "load_bound": {"bound": "latency: the routing replays the prompt's decisions in order in one CTA",
+                          "kv_bytes_moved": moved}}
+    if cpu_sample > 0:
+        import numpy as np
+        from oracle.graph_cache import ClusterGeometry, GraphOracle
+        o = GraphOracle(ClusterGeometry(L, H, D, w["n_clusters"], w["cap"], w["threshold"], w["sink"], w["recent"]))
+        kn = k[:, :, :cpu_sample].float().cpu().numpy()
+        vn = v[:, :, :cpu_sample].float().cpu().numpy()
+        sn = scores[:cpu_sample].cpu().numpy()
+        t0 = time.perf_counter()
+        o.load_from_summary(kn, vn, sn)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": cpu_sample / dt, "unit": "prompt tokens/s (load_from_summary)", "cores": 1,
+                               "kind": "port", "sample": f"the first {cpu_sample} prompt tokens"}
+    del c, k, v
+    return out
+
+
 C3_WORKLOAD = dict(layers=28, hq=28, hkv=4, d=128, sessions=64, min_prompt=1024, max_prompt=8192, sink=4,
                    recent=512, important=1532, dtype="float16", decay=0.99, seed=2)
 C3_ALG_BYTES_PER_SESSION_LAYER = 4_227_584  # K/V 4,194,304 + append 2,048 + q/o 14,336 + table 512 + importance 16,384
@@ -534,7 +616,7 @@ def main():
     h2d, d2h = stepper.h2d_bytes, stepper.d2h_bytes
     b.check_device_status()
 
-    summ = paged = c3 = None
+    summ = paged = c3 = graph = None
     if not args.no_summary:
         log("summary leg")
         summ = summary_leg(device)
@@ -542,6 +624,8 @@ def main():
         paged = paged_leg(device)
         log("7b-shaped decode leg")
         c3 = config3_leg(device)
+        log("graph cache leg")
+        graph = graph_leg(device, cpu_sample=256 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -568,7 +652,8 @@ def main():
                 "cuda_graph": not args.no_graph,
                 "summary_score": summ,
                 "paged_gather": paged,
-                "decode_7b_shape": c3}
+                "decode_7b_shape": c3,
+                "graph_cache": graph}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphs

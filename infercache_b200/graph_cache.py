@@ -15,7 +15,8 @@ Everything lives on the device in one slot store (``ic_graph_state``): a
 push of one token, or a bulk ``load_from_summary`` of a whole prompt, is one
 routing launch (the sequential decisions, on the layer-0 / head-0 keys only)
 plus a parallel copy of every layer's and head's K/V rows; ``retrieve`` is
-one selection launch plus one row gather per layer.  There is no CPU path.
+one selection launch plus one row gather each for K and V over all layers.
+There is no CPU path.
 """
 from __future__ import annotations
 
@@ -156,17 +157,17 @@ class GraphKVCache:
             return None, selected
         idx = self._slots[:F].to(torch.int64)
         dev = device or self.device
-        out = []
-        for li in range(cfg.num_layers):
-            K = torch.empty((cfg.num_kv_heads, F, cfg.head_dim), dtype=cfg.dtype, device=self.device)
-            V = torch.empty_like(K)
-            for src, dst in ((self.K[li], K), (self.V[li], V)):
-                ga = _lib.ic_index_rows_args(src=src.data_ptr(), out=dst.data_ptr(), idx=idx.data_ptr(),
-                                             stride_h=src.stride(0), stride_n=src.stride(1), H=cfg.num_kv_heads,
-                                             N=src.shape[1], F=F, D=cfg.head_dim, dtype=_lib.dtype_code(cfg.dtype))
-                _lib.call("ic_index_rows", ga)
-            out.append((K[None].to(dev), V[None].to(dev)))
-        return tuple(out), selected
+        # one row gather per store over all (layer, head) planes
+        LH, NS = cfg.num_layers * cfg.num_kv_heads, cfg.total_budget
+        K = torch.empty((cfg.num_layers, cfg.num_kv_heads, F, cfg.head_dim), dtype=cfg.dtype, device=self.device)
+        V = torch.empty_like(K)
+        for src, dst in ((self.K, K), (self.V, V)):
+            ga = _lib.ic_index_rows_args(src=src.data_ptr(), out=dst.data_ptr(), idx=idx.data_ptr(),
+                                         stride_h=NS * cfg.head_dim, stride_n=cfg.head_dim, H=LH, N=NS, F=F,
+                                         D=cfg.head_dim, dtype=_lib.dtype_code(cfg.dtype))
+            _lib.call("ic_index_rows", ga)
+        K, V = K.to(dev), V.to(dev)
+        return tuple((K[li][None], V[li][None]) for li in range(cfg.num_layers)), selected
 
     def retrieve_positions(self, query_key: torch.Tensor, threshold: Optional[float] = None,
                            top_n_clusters: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
