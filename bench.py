@@ -372,6 +372,9 @@ def graph_leg(device, iters=5, cpu_sample=0):
     return out
 
 
+STEPS_PER_GRAPH = 4  # decode steps per replayed CUDA graph in the timed region
+
+
 C3_WORKLOAD = dict(layers=28, hq=28, hkv=4, d=128, sessions=64, min_prompt=1024, max_prompt=8192, sink=4,
                    recent=512, important=1532, dtype="float16", decay=0.99, seed=2)
 C3_ALG_BYTES_PER_SESSION_LAYER = 4_227_584  # K/V 4,194,304 + append 2,048 + q/o 14,336 + table 512 + importance 16,384
@@ -528,6 +531,10 @@ def main():
             b.attend(l, q[l], k[l], v[l], out=out[l])
 
     run_step, run_dec = eager_step, eager_dec
+
+    def run_multi():
+        for _ in range(STEPS_PER_GRAPH):
+            eager_step()
     graphs = []
     if not args.no_graph:
         # one decode step of every session, captured once and replayed
@@ -537,11 +544,19 @@ def main():
         step_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(step_graph, stream=cap):
             eager_step()
+        # STEPS_PER_GRAPH consecutive steps in one graph: the eviction kernel of
+        # one step and the first layer of the next stay in one graph, linked by
+        # programmatic dependent launch, instead of meeting at a graph boundary
+        multi_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(multi_graph, stream=cap):
+            for _ in range(STEPS_PER_GRAPH):
+                eager_step()
         dec_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(dec_graph, stream=cap):
             eager_dec()
-        graphs = [step_graph, dec_graph]
+        graphs = [step_graph, multi_graph, dec_graph]
         run_step, run_dec = step_graph.replay, dec_graph.replay
+        run_multi = multi_graph.replay
     log("graph warm-up")
     for _ in range(args.warmup):
         run_step()
@@ -555,7 +570,9 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(args.steps // STEPS_PER_GRAPH):
+        run_multi()
+    for _ in range(args.steps % STEPS_PER_GRAPH):
         run_step()
     e1.record()
     torch.cuda.synchronize()
@@ -649,7 +666,8 @@ def main():
                                "(one CUDA graph per step; the output copy of step i overlaps step i + 1)"},
                 "gpu_launches": args.steps * (L + 1),
                 "clocks": sampler.summary() if sampler else None,
-                "cuda_graph": not args.no_graph,
+                "cuda_graph": (f"{STEPS_PER_GRAPH} steps per graph (remainder: 1 per graph)"
+                               if not args.no_graph else False),
                 "summary_score": summ,
                 "paged_gather": paged,
                 "decode_7b_shape": c3,
