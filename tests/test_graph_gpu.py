@@ -91,3 +91,71 @@ def test_graph_cache_push_after_load_and_reset():
     assert a.active_cluster_count == 0 and bool((a.positions == -1).all()) and not a.K.any()
     pkv, sel = a.retrieve(torch.randn(sp["H"], sp["D"]))
     assert pkv is None and sel.sum() == 1
+
+
+GEOMETRIES = [
+    # (L, H, n_clusters, cap, sink, recent, threshold, T)
+    (1, 1, 1, 1, 0, 1, 0.3, 40),      # one cluster of one slot, ring of one, no sinks
+    (2, 2, 3, 2, 4, 2, 0.0, 60),      # threshold 0: any positive similarity routes
+    (2, 1, 5, 4, 2, 3, 0.99, 80),     # threshold near 1: mostly first-empty / least-filled
+    (1, 2, 8, 3, 4, 5, 0.3, 3),       # fewer tokens than sinks
+    (3, 2, 2, 16, 1, 7, 0.5, 150),
+]
+
+
+@pytest.mark.parametrize("geo", GEOMETRIES)
+def test_graph_random_geometries_vs_oracle(geo):
+    """Edge geometries against the oracle, pushed one token at a time and
+    loaded in bulk.  Inputs whose routing would come within 5e-5 of a tie or
+    the threshold are redrawn (the decision would then depend on how a cosine
+    is summed)."""
+    from infercache_b200 import ClusterConfig, GraphKVCache
+    from oracle.graph_cache import ClusterGeometry, GraphOracle
+    L, H, C, cap, sink, recent, thr, T = geo
+    D = 128
+    for seed in range(50):
+        g = torch.Generator().manual_seed(1000 + seed)
+        dirs = torch.randn(4, D, generator=g)
+        dirs = dirs / dirs.norm(dim=1, keepdim=True)
+        k = torch.randn(L, H, T, D, generator=g)
+        k[0, 0] = dirs[torch.randint(0, 4, (T,), generator=g)] * 3.0 + torch.randn(T, D, generator=g)
+        k, v = k.half(), torch.randn(L, H, T, D, generator=g).half()
+        scores = torch.rand(T, generator=g)
+        o = GraphOracle(ClusterGeometry(L, H, D, C, cap, thr, sink, recent))
+        kn, vn = k.float().numpy(), v.float().numpy()
+        margins = []
+        for t in range(T):
+            if not (t < sink and o.sink_fill < sink) and o.rec_pos[o.rec_ptr] >= 0:
+                margins.append(o.route_margin(o.rec_k[0, 0, o.rec_ptr].astype(np.float32)))
+            o.push(kn[:, :, t], vn[:, :, t], t, float(scores[t]))
+        if not margins or min(margins) > 5e-5:
+            break
+    cfg = ClusterConfig(num_layers=L, num_kv_heads=H, head_dim=D, n_clusters=C, cluster_capacity=cap,
+                        sim_threshold=thr, sink_size=sink, recent_size=recent)
+    one = GraphKVCache(cfg, "cuda:0")
+    bulk = GraphKVCache(cfg, "cuda:0")
+    for t in range(T):
+        one.push(k[:, :, t:t + 1].cuda(), v[:, :, t:t + 1].cuda(), t, float(scores[t]))
+    bulk.load_from_summary(tuple((k[li][None].cuda(), v[li][None].cuda()) for li in range(L)), scores.cuda())
+    want = np.concatenate([o.sink_pos, o.rec_pos, o.cl_pos.reshape(-1)])
+    for c in (one, bulk):
+        assert np.array_equal(c.positions.cpu().numpy(), want)
+        assert np.array_equal(c.centroid.cpu().numpy(), o.centroid)
+        assert np.array_equal(c.scores.cpu().numpy(), o.cl_score.reshape(-1))
+        assert np.array_equal(c.cl_fill.cpu().numpy(), o.cl_fill)
+        pos = c.positions.cpu().numpy()
+        occ = np.nonzero(pos >= 0)[0]
+        assert torch.equal(c.K.cpu()[:, :, occ], k[:, :, pos[occ]])
+    for key in ("positions", "scores", "centroid", "cl_fill", "c_count", "ctrl", "K", "V"):
+        assert torch.equal(getattr(one, key), getattr(bulk, key)), key
+
+
+def test_graph_push_of_nothing_and_bad_shapes():
+    from infercache_b200 import ClusterConfig, GraphKVCache
+    cfg = ClusterConfig(num_layers=2, num_kv_heads=2, head_dim=128, n_clusters=2, cluster_capacity=2, recent_size=2)
+    c = GraphKVCache(cfg, "cuda:0")
+    c._push_many(torch.zeros(2, 2, 0, 128), torch.zeros(2, 2, 0, 128), torch.zeros(0, dtype=torch.int64), None,
+                 reset=False)
+    assert bool((c.positions == -1).all())
+    with pytest.raises(ValueError):
+        c.push(torch.zeros(3, 2, 1, 128), torch.zeros(3, 2, 1, 128), 0)
