@@ -492,6 +492,9 @@ class HostStepper:
     this step's output; ``wait(index)`` (or ``synchronize()``) makes it
     readable.
 
+    When q_host, k_host and v_host lie back to back in one pinned block (one
+    dtype), the step uploads the block with a single copy.
+
     ``zero_copy`` makes the decode kernels read q / k / v from, and write the
     output to, the pinned host buffers themselves (mapped host memory over
     PCIe): no staging copies and no copy launches, at the price of PCIe
@@ -550,9 +553,24 @@ class HostStepper:
             self._used = [False] * len(outs)
             self._next = 0
             return
-        self._q = torch.empty(q_host.shape, dtype=q_host.dtype, device=dev)
-        self._k = torch.empty(k_host.shape, dtype=k_host.dtype, device=dev)
-        self._v = torch.empty(v_host.shape, dtype=v_host.dtype, device=dev)
+        # q, k and v back to back in one host block (same dtype): one upload of
+        # the block into a device block with the same layout
+        nq, nk, nv = q_host.numel(), k_host.numel(), v_host.numel()
+        esz = q_host.element_size()
+        self.packed_inputs = (q_host.dtype == k_host.dtype == v_host.dtype and
+                              k_host.data_ptr() == q_host.data_ptr() + nq * esz and
+                              v_host.data_ptr() == k_host.data_ptr() + nk * esz)
+        if self.packed_inputs:
+            block = torch.empty(nq + nk + nv, dtype=q_host.dtype, device=dev)
+            self._q = block[:nq].view(q_host.shape)
+            self._k = block[nq:nq + nk].view(k_host.shape)
+            self._v = block[nq + nk:].view(v_host.shape)
+            host_block = torch.empty(0, dtype=q_host.dtype).set_(
+                q_host.untyped_storage(), q_host.storage_offset(), (nq + nk + nv,), (1,))
+        else:
+            self._q = torch.empty(q_host.shape, dtype=q_host.dtype, device=dev)
+            self._k = torch.empty(k_host.shape, dtype=k_host.dtype, device=dev)
+            self._v = torch.empty(v_host.shape, dtype=v_host.dtype, device=dev)
         self._o = [torch.empty(o.shape, dtype=o.dtype, device=dev) for o in outs]
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in (q_host, k_host, v_host))
         self.d2h_bytes = outs[0].numel() * outs[0].element_size()
@@ -563,9 +581,12 @@ class HostStepper:
             gr = torch.cuda.CUDAGraph()
             # relaxed: the first launch of each kernel may set its shared-memory limit
             with torch.cuda.graph(gr, stream=cap, capture_error_mode="relaxed"):
-                self._q.copy_(q_host, non_blocking=True)
-                self._k.copy_(k_host, non_blocking=True)
-                self._v.copy_(v_host, non_blocking=True)
+                if self.packed_inputs:
+                    block.copy_(host_block, non_blocking=True)
+                else:
+                    self._q.copy_(q_host, non_blocking=True)
+                    self._k.copy_(k_host, non_blocking=True)
+                    self._v.copy_(v_host, non_blocking=True)
                 batch.step(self._q, self._k, self._v, positions, out=self._o[k])
                 positions.add_(1)
                 if not self.pipelined:

@@ -104,6 +104,33 @@ def test_pipelined_host_stepper_matches_eager_steps():
         assert torch.equal(getattr(a, key), getattr(b, key)), key
 
 
+def test_packed_input_host_stepper_matches_eager_steps():
+    """q / k / v as views of one pinned block: one upload per step, same
+    outputs and cache state as eager steps."""
+    a = _batch(3, seed=19)
+    b = _batch(3, seed=19)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn(3, 3, 16, 128, generator=g, device="cuda").half()
+    k = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    v = torch.randn(3, 3, 2, 128, generator=g, device="cuda").half()
+    block = torch.empty(q.numel() + k.numel() + v.numel(), dtype=torch.float16).pin_memory()
+    qh = block[:q.numel()].view(q.shape)
+    kh = block[q.numel():q.numel() + k.numel()].view(k.shape)
+    vh = block[q.numel() + k.numel():].view(v.shape)
+    qh.copy_(q.cpu()); kh.copy_(k.cpu()); vh.copy_(v.cpu())
+    pos = torch.full((3,), 600, dtype=torch.int64, device="cuda")
+    ohs = tuple(torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(2))
+    st = b.host_stepper(qh, kh, vh, ohs, pos)
+    assert st.packed_inputs
+    for i in range(8):
+        ref = a.step(q, k, v, torch.full((3,), 600 + i, dtype=torch.int64, device="cuda")).cpu()
+        idx = st.run()
+        st.wait(idx)
+        assert torch.equal(ohs[idx], ref), i
+    for key in ("positions", "importance", "occupied", "ctrl", "counters"):
+        assert torch.equal(getattr(a, key), getattr(b, key)), key
+
+
 def test_zero_copy_host_stepper_matches_eager_steps():
     """The stepper whose kernels read and write the pinned host buffers
     directly (zero_copy) gives the same outputs and cache state as eager
