@@ -468,9 +468,9 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="replay steps eagerly instead of as a CUDA graph")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-summary", action="store_true",
-                    help="skip the secondary legs (summary scorer, paged gather, 7B-shaped decode)")
-    ap.add_argument("--workload", choices=["decode", "summary"], default="decode",
-                    help="summary: time only the summary-pass scorer (for profiling)")
+                    help="skip the secondary legs (summary scorer, paged gather, 7B-shaped decode, graph cache)")
+    ap.add_argument("--workload", choices=["decode", "summary", "graph"], default="decode",
+                    help="summary / graph: time only the summary-pass scorer / the graph cache (for profiling)")
     ap.add_argument("--summary-batch", type=int, default=0, help="sequences in the summary workload")
     args = ap.parse_args()
     faulthandler.enable()
@@ -487,6 +487,10 @@ def main():
     if args.workload == "summary":
         if rank == 0:
             print(json.dumps(summary_leg(device, iters=args.steps, batch=args.summary_batch or None)), flush=True)
+        return
+    if args.workload == "graph":
+        if rank == 0:
+            print(json.dumps(graph_leg(device, iters=max(1, min(args.steps, 20)))), flush=True)
         return
     if world > 1:
         from datetime import timedelta
