@@ -414,8 +414,7 @@ def config3_leg(device, steps=20, warmup=3):
     cap.wait_stream(torch.cuda.current_stream())
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gr, stream=cap):
-        b.step(q, k, v, pos, out=out)
-        pos.add_(1)
+        b.step(q, k, v, pos, out=out, advance_positions=True)
     for _ in range(warmup):
         gr.replay()
     torch.cuda.synchronize()
@@ -527,8 +526,7 @@ def main():
     torch.cuda.synchronize()
 
     def eager_step():
-        b.step(q, k, v, pos, out=out)
-        pos.add_(1)
+        b.step(q, k, v, pos, out=out, advance_positions=True)
 
     def eager_dec():
         for l in range(L):

@@ -183,7 +183,8 @@ typedef struct ic_evict_args {
   float mass_div;
   float decay;
   int32_t pdl;             /* 1: launch with programmatic dependent launch */
-  const int64_t* new_pos;  /* [S] */
+  int32_t advance_pos;     /* 1: new_pos[s] += 1 once read (the next step's position) */
+  int64_t* new_pos;        /* [S] */
   int64_t* events;         /* [S, 4] record of this step, or NULL */
 } ic_evict_args;
 int ic_evict_update(const ic_evict_args* a, void* stream);

@@ -85,7 +85,7 @@ class ic_decode_args(Structure):
 class ic_evict_args(Structure):
     _fields_ = [("tiers", ic_tiers), ("sess", ic_sessions), ("mass", c_void_p), ("mass_heads", c_int32),
                 ("mass_layers", c_int32), ("mass_div", c_float), ("decay", c_float), ("pdl", c_int32),
-                ("new_pos", c_void_p), ("events", c_void_p)]
+                ("advance_pos", c_int32), ("new_pos", c_void_p), ("events", c_void_p)]
 
 
 class ic_graph_state(Structure):

@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
     snap_fill = ctrl[IC_CTRL_IMPORTANT_FILL];
     snap_rf = ctrl[IC_CTRL_RECENT_FILL];
     snap_newpos = a.new_pos[s];
+    if (a.advance_pos) a.new_pos[s] = snap_newpos + 1;  // the next step's position
     for (int i = 0; i < IC_COUNTER_WORDS; ++i) snap_cnt[i] = cnt[i];
     const bool ok = snap_r >= sink && snap_r < l2s && snap_fill >= 0 && snap_fill <= cap;
     if (!ok) {

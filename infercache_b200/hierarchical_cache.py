@@ -221,14 +221,19 @@ class SessionBatch:
         e.mass_layers = 1
         e.mass_div = float(self.cfg.num_layers * self.cfg.num_kv_heads)
         e.pdl = 1 if self.pdl else 0
+        e.advance_pos = 0
         _lib.call("ic_evict_update", e)
         self._keep = pos  # keep alive until the launch is consumed
 
     def step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions,
-             out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+             out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+             advance_positions: bool = False) -> torch.Tensor:
         """One decode step of every session in one C call (``ic_decode_step``):
         q [L, S, Hq, D], k / v [L, S, Hkv, D] contiguous in the cache dtype;
-        positions [S] of the decoded tokens.  Returns out [L, S, Hq, D]."""
+        positions [S] of the decoded tokens.  Returns out [L, S, Hq, D].
+        ``advance_positions`` (positions an int64 tensor on this device): the
+        eviction kernel adds one to each session's position once it has read
+        it, so consecutive steps need no separate increment launch."""
         cfg = self.cfg
         L, S, D = cfg.num_layers, self.num_sessions, cfg.head_dim
         if q.dim() != 4 or q.shape[0] != L or q.shape[1] != S or q.shape[3] != D:
@@ -253,6 +258,10 @@ class SessionBatch:
         d.out = out.data_ptr()
         d.out_dtype = _lib.dtype_code(out.dtype)
         st.evict.pdl = 1 if self.pdl else 0
+        if advance_positions and not (isinstance(positions, torch.Tensor) and positions.device == self.device
+                                      and positions.dtype == torch.int64 and positions.is_contiguous()):
+            raise ValueError("advance_positions needs positions as a contiguous int64 tensor on the cache device")
+        st.evict.advance_pos = 1 if advance_positions else 0
         st.q_layer_stride = S * Hq * D
         st.kv_layer_stride = S * cfg.num_kv_heads * D
         st.out_layer_stride = S * Hq * D
@@ -265,7 +274,8 @@ class SessionBatch:
     def _step_raw(self, q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, num_q_heads: int,
                   out_dtype: torch.dtype, pos: torch.Tensor) -> None:
         """``step`` on raw device addresses of contiguous [L, S, H, D] buffers
-        in the cache dtype (e.g. mapped pinned host memory); no checks."""
+        in the cache dtype (e.g. mapped pinned host memory), advancing the
+        positions; no checks."""
         cfg = self.cfg
         S, D = self.num_sessions, cfg.head_dim
         st = self._step
@@ -274,6 +284,7 @@ class SessionBatch:
         d.q, d.k_new, d.v_new, d.out = q_ptr, k_ptr, v_ptr, out_ptr
         d.out_dtype = _lib.dtype_code(out_dtype)
         st.evict.pdl = 1 if self.pdl else 0
+        st.evict.advance_pos = 1
         st.q_layer_stride = S * num_q_heads * D
         st.kv_layer_stride = S * cfg.num_kv_heads * D
         st.out_layer_stride = S * num_q_heads * D
@@ -544,7 +555,6 @@ class HostStepper:
                 gr = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gr, stream=cap, capture_error_mode="relaxed"):
                     batch._step_raw(qd, kd, vd, ods[k], Hq, outs[k].dtype, positions)
-                    positions.add_(1)
                 self.graphs.append(gr)
             self.graph = self.graphs[0]
             self._copy = None
@@ -587,8 +597,7 @@ class HostStepper:
                     self._q.copy_(q_host, non_blocking=True)
                     self._k.copy_(k_host, non_blocking=True)
                     self._v.copy_(v_host, non_blocking=True)
-                batch.step(self._q, self._k, self._v, positions, out=self._o[k])
-                positions.add_(1)
+                batch.step(self._q, self._k, self._v, positions, out=self._o[k], advance_positions=True)
                 if not self.pipelined:
                     outs[0].copy_(self._o[0], non_blocking=True)
             self.graphs.append(gr)

@@ -224,6 +224,37 @@ def test_config2_full_size(variant):
     b1.check_device_status()
 
 
+def test_step_advancing_positions_in_kernel():
+    """advance_positions: kernel B adds one to every session's position after
+    reading it; steps driven that way match steps given explicit positions."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    cfg = CacheConfig(num_layers=2, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=8, important_size=12,
+                      decay=0.99, dtype=torch.float16)
+    g = torch.Generator().manual_seed(23)
+    pk = torch.randn(2, 2, 2, 50, 128, generator=g).half()
+    pv = torch.randn(2, 2, 2, 50, 128, generator=g).half()
+    sc = torch.rand(50, generator=g)
+    bs = []
+    for _ in range(2):
+        b = SessionBatch(cfg, 2, "cuda:0")
+        for s in range(2):
+            b.load_prompt(s, tuple((pk[l][s][None].cuda(), pv[l][s][None].cuda()) for l in range(2)), sc)
+        bs.append(b)
+    q = torch.randn(6, 2, 2, 16, 128, generator=g).half().cuda()
+    k = torch.randn(6, 2, 2, 2, 128, generator=g).half().cuda()
+    v = torch.randn(6, 2, 2, 2, 128, generator=g).half().cuda()
+    pos = torch.tensor([50, 70], dtype=torch.int64, device="cuda")
+    for t in range(6):
+        o1 = bs[0].step(q[t], k[t], v[t], [50 + t, 70 + t])
+        o2 = bs[1].step(q[t], k[t], v[t], pos, advance_positions=True)
+        assert torch.equal(o1, o2), t
+    assert pos.tolist() == [56, 76]
+    for key in ("positions", "importance", "occupied", "slot_table", "counters"):
+        assert torch.equal(getattr(bs[0], key), getattr(bs[1], key)), key
+    with pytest.raises(ValueError):
+        bs[1].step(q[0], k[0], v[0], [1, 2], advance_positions=True)
+
+
 def test_cluster_sizes_agree():
     """8- and 16-CTA clusters differ only in float summation order."""
     from infercache_b200 import CacheConfig, SessionBatch
