@@ -357,7 +357,6 @@ def graph_leg(device, iters=5, cpu_sample=0):
            "load_bound": {"bound": "latency: the routing replays the prompt's decisions in order in one CTA",
                           "kv_bytes_moved": moved}}
     if cpu_sample > 0:
-        import numpy as np
         from oracle.graph_cache import ClusterGeometry, GraphOracle
         o = GraphOracle(ClusterGeometry(L, H, D, w["n_clusters"], w["cap"], w["threshold"], w["sink"], w["recent"]))
         kn = k[:, :, :cpu_sample].float().cpu().numpy()
