@@ -78,6 +78,8 @@ class GraphKVCache:
         self._slots = torch.empty(NS, dtype=torch.int32, device=dev)
         self._count = torch.zeros(1, dtype=torch.int32, device=dev)
         self._selected = torch.zeros(C, dtype=torch.uint8, device=dev)
+        self._pos1 = torch.zeros(1, dtype=torch.int64, device=dev)    # a single push's position and score,
+        self._score1 = torch.zeros(1, dtype=torch.float32, device=dev)  # set on the device (no host copy)
         self._state = _lib.ic_graph_state(
             k=self.K.data_ptr(), v=self.V.data_ptr(), positions=self.positions.data_ptr(),
             scores=self.scores.data_ptr(), centroid=self.centroid.data_ptr(), cl_fill=self.cl_fill.data_ptr(),
@@ -123,8 +125,9 @@ class GraphKVCache:
     def push(self, key_states: torch.Tensor, value_states: torch.Tensor, position: int,
              score: float = 0.0) -> None:
         """graph_cache.py:287-323: key_states / value_states [L, H, 1, D]."""
-        self._push_many(key_states, value_states, torch.tensor([int(position)], dtype=torch.int64),
-                        torch.tensor([float(score)], dtype=torch.float32), reset=False)
+        self._pos1.fill_(int(position))
+        self._score1.fill_(float(score))
+        self._push_many(key_states, value_states, self._pos1, self._score1, reset=False)
 
     def load_from_summary(self, past_key_values, importance_scores: torch.Tensor,
                           positions: Optional[torch.Tensor] = None) -> None:
