@@ -194,11 +194,14 @@ def measured_tensor_peak():
 SUMMARY_WORKLOAD = dict(batch=8, hq=16, hkv=2, T=8192, d=128)
 
 
-def summary_leg(device, iters=10, batch=None):
+def summary_leg(device, iters=10, batch=None, cpu_tokens=0):
     """Kernel C on the summary-pass workload: 8 sequences x 16/2 heads x 8192
     tokens, causal, bf16 (seeded synthetic q / k / v).  Algorithmic work is the
     causal QK^T + PV: 4 * B * Hq * D * T (T + 1) / 2 flops; the column-sum
-    sweep's extra QK^T is overhead, not work."""
+    sweep's extra QK^T is overhead, not work.  With cpu_tokens > 0 the oracle's
+    restatement of _attention_mass times one sequence of that many tokens on
+    the host (the mass only; the reference materialises P, as the oracle
+    does a chunk at a time)."""
     from infercache_b200.summary import summary_score
     w = SUMMARY_WORKLOAD
     B, Hq, Hkv, T, D = batch or w["batch"], w["hq"], w["hkv"], w["T"], w["d"]
@@ -223,12 +226,26 @@ def summary_leg(device, iters=10, batch=None):
     flops = 4 * B * Hq * D * T * (T + 1) / 2
     peak, kind = measured_tensor_peak()
     tflops = flops / (ms / 1e3) / 1e12
+    out = {"workload": f"summary pass: {B} sequences x {Hq}/{Hkv} heads x {T} tokens causal, head_dim {D}, bf16",
+           "kernels": "summary_fwd_kernel + summary_colsum_kernel + summary_head_sum_kernel + summary_normalise_kernel (ic_summary_score)",
+           "ms_per_call": ms, "alg_tflop_per_call": flops / 1e12,
+           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                        "frac": tflops / peak, "peak_kind": f"{kind} (MEASURED_PEAKS.json bf16_tflops, burst)"}}
+    if cpu_tokens > 0:
+        from oracle.summary import attention_mass
+        Tc = min(cpu_tokens, T)
+        qc = q[0, :, :Tc].float().cpu().numpy()
+        kc = k[0, :, :Tc].float().cpu().numpy()
+        t0 = time.perf_counter()
+        attention_mass(qc, kc, D ** -0.5)
+        dt = time.perf_counter() - t0
+        cflops = 2 * Hq * D * Tc * (Tc + 1) / 2  # the causal QK^T the mass needs
+        out["cpu_baseline"] = {"value": Tc / dt, "unit": "prompt tokens/s (attention mass, one sequence)",
+                               "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": f"one sequence of {Tc} tokens, {Hq}/{Hkv} heads (numpy, {cflops / dt / 1e9:.1f} GFLOP/s)",
+                               "gpu_same_unit": B * T / (ms / 1e3)}
     del q, k, v
-    return {"workload": f"summary pass: {B} sequences x {Hq}/{Hkv} heads x {T} tokens causal, head_dim {D}, bf16",
-            "kernels": "summary_fwd_kernel + summary_colsum_kernel + summary_head_sum_kernel + summary_normalise_kernel (ic_summary_score)",
-            "ms_per_call": ms, "alg_tflop_per_call": flops / 1e12,
-            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
-                         "frac": tflops / peak, "peak_kind": f"{kind} (MEASURED_PEAKS.json bf16_tflops, burst)"}}
+    return out
 
 
 PAGED_WORKLOAD = dict(sessions=16, min_len=256, max_len=32768, layers=36, heads=2, d=128, seed=4)
@@ -644,7 +661,7 @@ def main():
     summ = paged = c3 = graph = None
     if not args.no_summary:
         log("summary leg")
-        summ = summary_leg(device)
+        summ = summary_leg(device, cpu_tokens=4096 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0)
         log("paged gather leg")
         paged = paged_leg(device)
         log("7b-shaped decode leg")
