@@ -9,13 +9,14 @@
 //     query tiles): S = Q K^T into TMEM (tcgen05.mma, operands staged by
 //     TMA), the row softmax in registers (one warpgroup per query tile, one
 //     thread per row, online max kept unless it grows by more than 2^8, so O
-//     is rescaled only then), P written as 16-bit to shared memory, O += P V
-//     into TMEM; epilogue O / l and the row log-sum-exp.
+//     is rescaled only then), P written back to TMEM as 16-bit, O += P V
+//     into TMEM (P read from TMEM); epilogue O / l and the row log-sum-exp.
 //  2. summary_colsum_kernel, one CTA per (sequence, query head, 128-key
 //     tile): S^T = K Q^T into TMEM for every query tile at or below the
 //     diagonal, then p = exp2(s * scale * log2 e - lse2) with one thread per
 //     key summing its column in fp32 registers — a fixed order, so the result
-//     is deterministic.
+//     is deterministic.  Part of the exponentials run on the FP32 pipe
+//     (exp2_poly.cuh), the rest on the multi-function unit.
 //  3. summary_head_sum_kernel: colsum = sum over heads in head order; then
 //     summary_normalise_kernel: the normalised importance with a fixed-shape
 //     block reduction.
@@ -29,6 +30,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "exp2_poly.cuh"
 #include "tc05.cuh"
 
 namespace ic {
@@ -113,6 +115,10 @@ constexpr int F_R = 2 * TILE;
 constexpr int F_BAR = F_R + FWD_RS * TILE;
 constexpr int F_NBAR = 20;
 constexpr int F_BYTES = F_BAR + F_NBAR * 8 + 16 + 1024;  // + alignment slack
+// Of every 8 column pairs, how many are exponentiated on the FP32 pipe.  0:
+// measured on B200, 2 or 3 slowed this kernel (its softmax threads already
+// sit at the 168-register cap of a 352-thread CTA).
+constexpr int FWD_POLY_PAIRS = 0;
 
 template <typename T, bool WITH_O>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
@@ -136,8 +142,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_pair = (p.n_t + 1) >> 1;
-  const int bh = blockIdx.x / n_pair;
-  const int qa = 2 * (n_pair - 1 - (int)(blockIdx.x % n_pair));  // longest rows first
+  const int n_bh = (int)gridDim.x / n_pair;
+  const int bh = (int)blockIdx.x % n_bh;
+  const int qa = 2 * (n_pair - 1 - (int)blockIdx.x / n_bh);  // longest rows first, over all heads
   const bool has_b = qa + 1 < p.n_t;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvz = b * p.Hkv + h / p.G;
@@ -284,16 +291,24 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.sl2;
       const float m_new = mx > m_used + RESCALE_LOG2 ? mx : m_used;
       const float alpha = m_new == m_used ? 1.f : tc::ex2(m_used - m_new);
-      float r4[4] = {0.f, 0.f, 0.f, 0.f};
+      // row sum in four chains (column c into chain c mod 4), two per f32x2 register
+      poly::f2 r2[2] = {poly::splat(0.f), poly::splat(0.f)};
+      const poly::f2 sl2 = poly::splat(p.sl2), neg_m = poly::splat(-m_new);
 #pragma unroll
       for (int c0 = 0; c0 < SB; c0 += 16) {
         float pk[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float e0 = tc::ex2(fmaf(s[c0 + 2 * i], p.sl2, -m_new));
-          const float e1 = tc::ex2(fmaf(s[c0 + 2 * i + 1], p.sl2, -m_new));
-          r4[(2 * i) & 3] += e0;
-          r4[(2 * i + 1) & 3] += e1;
+        for (int i = 0; i < 8; ++i) {  // columns c0 + 2i, c0 + 2i + 1
+          const poly::f2 x = poly::fma2(poly::pack(s[c0 + 2 * i], s[c0 + 2 * i + 1]), sl2, neg_m);
+          float e0, e1;
+          if (i < FWD_POLY_PAIRS) {
+            poly::unpack(poly::exp2x2(x), e0, e1);
+          } else {
+            poly::unpack(x, e0, e1);
+            e0 = tc::ex2(e0);
+            e1 = tc::ex2(e1);
+          }
+          r2[i & 1] = poly::add2(r2[i & 1], poly::pack(e0, e1));
           if (WITH_O) pk[i] = __uint_as_float(pack2(e0, e1, (T*)nullptr));
         }
         if (WITH_O) {
@@ -305,6 +320,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         }
       }
       if (!ok) break;
+      float r4[4];
+      poly::unpack(r2[0], r4[0], r4[1]);
+      poly::unpack(r2[1], r4[2], r4[3]);
       l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
       if (WITH_O) {
         if (j >= 1 && __any_sync(0xffffffffu, m_new != m_used)) {
@@ -372,6 +390,9 @@ constexpr int C_RED = C_LSE + COL_NS * SB * 4;
 constexpr int C_BAR = C_RED + SB * 4;
 constexpr int C_NBAR = 20;
 constexpr int C_BYTES = C_BAR + C_NBAR * 8 + 16 + 1024;
+// Of every 8 query pairs, how many are exponentiated on the FP32 pipe: 2
+// (measured on B200 against 0 and 3: 3.6% and 4.2% less kernel time).
+constexpr int COL_POLY_PAIRS = 2;
 
 template <typename T>
 __global__ void __launch_bounds__(COL_THREADS, 1)
@@ -389,13 +410,15 @@ __global__ void __launch_bounds__(COL_THREADS, 1)
   uint64_t* mma_done = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C_BAR + C_NBAR * 8);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C_BAR + C_NBAR * 8 + 4);
-  float* lse_s = reinterpret_cast<float*>(smem + C_LSE);  // [4][128], log2 units
+  float* lse_s = reinterpret_cast<float*>(smem + C_LSE);  // [4][128], -lse in log2 units
   float* red = reinterpret_cast<float*>(smem + C_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = p.n_t;
+  // (sequence, head)-major, so the CTAs running at once share one head's Q
+  // tiles in L2; longest columns first within a head
   const int bh = blockIdx.x / n_t;
-  const int kt = (int)(blockIdx.x % n_t);  // longest columns first
+  const int kt = (int)(blockIdx.x % n_t);
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvz = b * p.Hkv + h / p.G;
   const int n = n_t - kt;  // query tiles at or below the diagonal: kt .. n_t-1
@@ -434,7 +457,7 @@ __global__ void __launch_bounds__(COL_THREADS, 1)
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int c = lane * 4 + u;
-        lse_s[st * SB + c] = i * SB + c < p.T ? lrow[c] * LOG2E : INFINITY;
+        lse_s[st * SB + c] = i * SB + c < p.T ? -lrow[c] * LOG2E : -INFINITY;
       }
       if (lane == 0) {
         mbar_arrive_expect_tx(q_full + st, TILE);
@@ -488,17 +511,35 @@ __global__ void __launch_bounds__(COL_THREADS, 1)
       tc::tmem_wait_ld();
       tc::fence_before();
       tc::mbar_arrive(s_free + st);
-      const float* ls = lse_s + st * SB;
+      const float* ls = lse_s + st * SB;  // -lse2 per query
       float a4[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains, summed in a fixed order
       if (t == 0) {  // diagonal tile: query c sees key r iff c >= r
 #pragma unroll
         for (int c = 0; c < SB; ++c) {
-          const float e = tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
+          const float e = tc::ex2(fmaf(s[c], p.sl2, ls[c]));
           a4[c & 3] += c >= r ? e : 0.f;
         }
       } else {
+        // pairs of queries; COL_POLY_PAIRS of every 8 pairs take 2^x on the
+        // FP32 pipe, the rest on the multi-function unit
+        const poly::f2 sl2 = poly::splat(p.sl2);
+        poly::f2 acc2[2] = {poly::splat(0.f), poly::splat(0.f)};
 #pragma unroll
-        for (int c = 0; c < SB; ++c) a4[c & 3] += tc::ex2(fmaf(s[c], p.sl2, -ls[c]));
+        for (int c = 0; c < SB; c += 2) {
+          const poly::f2 x =
+              poly::fma2(poly::pack(s[c], s[c + 1]), sl2, *reinterpret_cast<const poly::f2*>(ls + c));
+          poly::f2 e;
+          if (((c >> 1) & 7) < COL_POLY_PAIRS) {
+            e = poly::exp2x2(x);
+          } else {
+            float x0, x1;
+            poly::unpack(x, x0, x1);
+            e = poly::pack(tc::ex2(x0), tc::ex2(x1));
+          }
+          acc2[(c >> 1) & 1] = poly::add2(acc2[(c >> 1) & 1], e);
+        }
+        poly::unpack(acc2[0], a4[0], a4[1]);
+        poly::unpack(acc2[1], a4[2], a4[3]);
       }
       acc += (a4[0] + a4[1]) + (a4[2] + a4[3]);
       tc::mbar_arrive(q_empty + st);
