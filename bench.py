@@ -7,7 +7,9 @@ with a 2048-token prompt into a 1040-slot budget (4 sink / 256 recent / 780
 important, 16-token pages), then decoded one token per step.  A step is one
 decode step of every session over every layer: 36 launches of the fused
 decode kernel (append + paged gather + GQA attention + received mass) and
-one launch of the eviction kernel.  Prompt K/V, importance scores and the
+one launch of the eviction kernel per session range -- the timed steps run
+the sessions as 8 ranges of 2, each range's steps a CUDA graph on its own
+stream, so one range's drain at a step boundary overlaps the others' work.  Prompt K/V, importance scores and the
 per-step q / k / v are seeded synthetic tensors (no model weights: the hot
 path is the cache, the model's projections are outside it).
 
@@ -389,6 +391,7 @@ def graph_leg(device, iters=5, cpu_sample=0):
 
 
 STEPS_PER_GRAPH = 4  # decode steps per replayed CUDA graph in the timed region
+SESSION_GROUPS = 8  # session ranges on their own streams in the timed region (SessionBatch.grouped_stepper)
 
 
 C3_WORKLOAD = dict(layers=28, hq=28, hkv=4, d=128, sessions=64, min_prompt=1024, max_prompt=8192, sink=4,
@@ -400,8 +403,8 @@ def config3_leg(device, steps=20, warmup=3):
     """The Qwen2.5-7B-shaped decode: 28 layers, 28/4 heads, head_dim 128,
     budget 2048 (4/512/1532), 64 sessions primed from prompts of U[1024, 8192]
     tokens (seed 2), fp16.  A step is one decode step of every session
-    (28 layer launches + kernel B), captured as a CUDA graph; 7.6 GB of K/V
-    per step, far above L2."""
+    (28 layer launches + kernel B per session range); 7.6 GB of K/V per step,
+    far above L2."""
     from infercache_b200 import CacheConfig, SessionBatch
     w = C3_WORKLOAD
     L, Hq, Hkv, D, S = w["layers"], w["hq"], w["hkv"], w["d"], w["sessions"]
@@ -426,30 +429,29 @@ def config3_leg(device, steps=20, warmup=3):
         b.step(q, k, v, pos, out=out)
         pos.add_(1)
     torch.cuda.synchronize()
-    cap = torch.cuda.Stream()
-    cap.wait_stream(torch.cuda.current_stream())
-    gr = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(gr, stream=cap):
-        b.step(q, k, v, pos, out=out, advance_positions=True)
-    for _ in range(warmup):
-        gr.replay()
+    # session ranges on their own streams, STEPS_PER_GRAPH steps per graph
+    gs = b.grouped_stepper(q, k, v, out, pos, groups=SESSION_GROUPS, steps_per_graph=STEPS_PER_GRAPH)
+    gs.run(max(1, warmup // STEPS_PER_GRAPH))
     torch.cuda.synchronize()
+    reps = max(1, steps // STEPS_PER_GRAPH)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(steps):
-        gr.replay()
+    gs.run(reps)
     e1.record()
     torch.cuda.synchronize()
     b.check_device_status()
+    steps = reps * STEPS_PER_GRAPH
     ms = e0.elapsed_time(e1) / steps
     alg = S * L * C3_ALG_BYTES_PER_SESSION_LAYER
     peak, kind = measured_peak()
     gbs = alg / (ms / 1e3) / 1e9
-    del gr, b, q, k, v, out
+    del gs, b, q, k, v, out
     return {"workload": f"qwen2.5-7b-shaped decode: {S} sessions x {L} layers, {Hq}/{Hkv} heads, head_dim {D}, "
                         f"budget 2048 (4/512/1532), prompts U[1024, 8192] (seed 2), fp16",
             "value": S / (ms / 1e3), "unit": "session-tokens/s", "ms_per_step": ms, "steps": steps,
             "alg_bytes_per_step": alg,
+            "cuda_graph": f"{STEPS_PER_GRAPH} steps per graph; {SESSION_GROUPS} session ranges of "
+                          f"{S // SESSION_GROUPS} on their own streams and graphs",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
 
@@ -481,6 +483,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cluster", type=int, default=0)
     ap.add_argument("--no-graph", action="store_true", help="replay steps eagerly instead of as a CUDA graph")
+    ap.add_argument("--session-groups", type=int, default=SESSION_GROUPS,
+                    help="session ranges stepped on their own streams and graphs in the timed region (1: one)")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-summary", action="store_true",
                     help="skip the secondary legs (summary scorer, paged gather, 7B-shaped decode, graph cache)")
@@ -513,6 +517,7 @@ def main():
 
     spec = dict(WORKLOAD)
     S, L, Hq, Hkv, D = spec["sessions"], spec["layers"], spec["hq"], spec["hkv"], spec["d"]
+    groups = 1 if args.no_graph else max(1, min(args.session_groups, S))
     log("priming sessions")
     b = build_batch(spec, device, seed=1234 + rank)
     b.cluster_size = args.cluster
@@ -550,8 +555,8 @@ def main():
 
     run_step, run_dec = eager_step, eager_dec
 
-    def run_multi():
-        for _ in range(STEPS_PER_GRAPH):
+    def run_multi(n=1):
+        for _ in range(n * STEPS_PER_GRAPH):
             eager_step()
     graphs = []
     if not args.no_graph:
@@ -574,10 +579,21 @@ def main():
             eager_dec()
         graphs = [step_graph, multi_graph, dec_graph]
         run_step, run_dec = step_graph.replay, dec_graph.replay
-        run_multi = multi_graph.replay
+
+        def run_multi(n=1):
+            for _ in range(n):
+                multi_graph.replay()
+        if groups > 1:
+            # the timed steps: session ranges on their own streams, each range's
+            # STEPS_PER_GRAPH steps one graph, so one range's step-boundary drain
+            # overlaps the others' streaming
+            grouped = b.grouped_stepper(q, k, v, out, pos, groups=groups, steps_per_graph=STEPS_PER_GRAPH)
+            graphs += grouped.graphs
+            run_multi = grouped.run
     log("graph warm-up")
     for _ in range(args.warmup):
         run_step()
+    run_multi()
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local_rank) if not args.no_clocks else None
@@ -588,8 +604,7 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps // STEPS_PER_GRAPH):
-        run_multi()
+    run_multi(args.steps // STEPS_PER_GRAPH)  # one join at the end, not per replay
     for _ in range(args.steps % STEPS_PER_GRAPH):
         run_step()
     e1.record()
@@ -689,10 +704,12 @@ def main():
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "steps": ke, "api": "SessionBatch.host_stepper: pinned q/k/v (one block) -> device, ic_decode_step, o -> pinned host "
                                "(one CUDA graph per step; the output copy of step i overlaps step i + 1)"},
-                "gpu_launches": args.steps * (L + 1),
+                "gpu_launches": (args.steps // STEPS_PER_GRAPH) * STEPS_PER_GRAPH * groups * (L + 1)
+                + (args.steps % STEPS_PER_GRAPH) * (L + 1),
                 "clocks": sampler.summary() if sampler else None,
                 "cuda_graph": (f"{STEPS_PER_GRAPH} steps per graph (remainder: 1 per graph)"
-                               if not args.no_graph else False),
+                               + (f"; {groups} session ranges of {S // groups} on their own streams and graphs"
+                                  if groups > 1 else "") if not args.no_graph else False),
                 "summary_score": summ,
                 "paged_gather": paged,
                 "decode_7b_shape": c3,

@@ -299,6 +299,12 @@ class SessionBatch:
         (see ``HostStepper``)."""
         return HostStepper(self, q_host, k_host, v_host, out_host, positions, zero_copy=zero_copy)
 
+    def grouped_stepper(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                        positions: torch.Tensor, groups: int = 8, steps_per_graph: int = 4) -> "GroupedStepper":
+        """Decode steps of every session with the sessions split into
+        ``groups`` ranges on their own streams (see ``GroupedStepper``)."""
+        return GroupedStepper(self, q, k, v, out, positions, groups=groups, steps_per_graph=steps_per_graph)
+
     def _positions_arg(self, positions) -> torch.Tensor:
         if isinstance(positions, torch.Tensor) and positions.device == self.device and positions.dtype == torch.int64:
             return positions.contiguous()
@@ -424,11 +430,14 @@ class SessionBatch:
         """ic_sessions for the single session row s."""
         if not 0 <= s < self.num_sessions:
             raise IndexError(s)
-        B = self.cfg.total_budget
-        return _lib.ic_sessions(num_sessions=1, slot_table=self.slot_table[s].data_ptr(),
-                                positions=self.positions[s].data_ptr(), importance=self.importance[s].data_ptr(),
-                                occupied=self.occupied[s].data_ptr(), ctrl=self.ctrl[s].data_ptr(),
-                                counters=self.counters[s].data_ptr(), dev_status=self.dev_status.data_ptr())
+        return self._range_sessions(s, s + 1)
+
+    def _range_sessions(self, s0: int, s1: int) -> _lib.ic_sessions:
+        """ic_sessions for the session rows s0 .. s1 - 1."""
+        return _lib.ic_sessions(num_sessions=s1 - s0, slot_table=self.slot_table[s0].data_ptr(),
+                                positions=self.positions[s0].data_ptr(), importance=self.importance[s0].data_ptr(),
+                                occupied=self.occupied[s0].data_ptr(), ctrl=self.ctrl[s0].data_ptr(),
+                                counters=self.counters[s0].data_ptr(), dev_status=self.dev_status.data_ptr())
 
     @staticmethod
     def _stats_from(c, n) -> CacheStats:
@@ -483,6 +492,96 @@ class StatsReadback:
     def result(self) -> List[CacheStats]:
         self._event.synchronize()
         return [SessionBatch._stats_from(c, n) for c, n in zip(self._ctrl.tolist(), self._cnt.tolist())]
+
+
+class GroupedStepper:
+    """Decode steps of every session of a batch, the sessions split into
+    ``groups`` contiguous ranges, each range's ``steps_per_graph`` steps
+    captured as its own CUDA graph (``ic_decode_step`` on that range, the
+    eviction kernel advancing the positions) and replayed on its own stream.
+
+    Within one stream the GPU drains at every step boundary: the eviction
+    kernel needs the step's last layer complete and the next step's first
+    layer needs the eviction.  Session ranges are independent, so ranges on
+    separate streams fill each other's drains.  Every kernel works per
+    session, so the results are bit-identical to ``SessionBatch.step``.
+
+    q / k / v / out: contiguous [L, S, H, D] device tensors in the cache dtype
+    (fixed: the graphs hold their addresses), positions: contiguous int64 [S]
+    on the device, advanced by one per step.  ``run(n)`` queues n replays
+    (n * steps_per_graph steps of every session) behind the work on the
+    current stream and makes the current stream wait for them; the streams
+    join only there, so queue many replays in one call.
+    """
+
+    def __init__(self, batch: SessionBatch, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                 positions: torch.Tensor, groups: int = 8, steps_per_graph: int = 4):
+        cfg = batch.cfg
+        L, S, D, Hkv = cfg.num_layers, batch.num_sessions, cfg.head_dim, cfg.num_kv_heads
+        if q.dim() != 4 or q.shape[0] != L or q.shape[1] != S or q.shape[3] != D:
+            raise ValueError(f"q must be [L={L}, S={S}, Hq, {D}], got {tuple(q.shape)}")
+        if tuple(k.shape) != (L, S, Hkv, D) or k.shape != v.shape:
+            raise ValueError(f"k / v must be [{L}, {S}, {Hkv}, {D}]")
+        if out.shape != q.shape:
+            raise ValueError("out must have q's shape")
+        for t in (q, k, v, out):
+            if t.dtype != cfg.dtype or t.device != batch.device or not t.is_contiguous():
+                raise ValueError("q / k / v / out must be contiguous tensors of the cache dtype on the cache device")
+        if not (isinstance(positions, torch.Tensor) and positions.device == batch.device
+                and positions.dtype == torch.int64 and positions.is_contiguous() and positions.numel() == S):
+            raise ValueError("positions must be a contiguous int64 [S] tensor on the cache device")
+        if not 1 <= int(groups) <= S or int(steps_per_graph) < 1:
+            raise ValueError("need 1 <= groups <= sessions and steps_per_graph >= 1")
+        self.batch, self.groups, self.steps_per_graph = batch, int(groups), int(steps_per_graph)
+        self._keep = (q, k, v, out, positions)
+        Hq = q.shape[2]
+        esz = q.element_size()
+        bounds = [S * g // self.groups for g in range(self.groups + 1)]
+        self.ranges = [(bounds[g], bounds[g + 1]) for g in range(self.groups)]
+        self._args = []
+        for s0, s1 in self.ranges:
+            d = _lib.ic_decode_args(pool=batch._c_pool, tiers=batch._c_tiers, sess=batch._range_sessions(s0, s1),
+                                    mass=batch.mass[s0].data_ptr(), scale=batch.scale)
+            batch._prepare_decode(d, Hq)
+            d.q = q.data_ptr() + s0 * Hq * D * esz
+            d.k_new = k.data_ptr() + s0 * Hkv * D * esz
+            d.v_new = v.data_ptr() + s0 * Hkv * D * esz
+            d.out = out.data_ptr() + s0 * Hq * D * esz
+            d.out_dtype = _lib.dtype_code(out.dtype)
+            e = _lib.ic_evict_args(tiers=batch._c_tiers, sess=batch._range_sessions(s0, s1),
+                                   mass=batch.mass[s0].data_ptr(), mass_heads=Hkv, mass_layers=1,
+                                   mass_div=float(L * Hkv), decay=cfg.decay, pdl=1 if batch.pdl else 0,
+                                   advance_pos=1, new_pos=positions[s0].data_ptr(), events=batch.events[s0].data_ptr())
+            self._args.append(_lib.ic_step_args(layer0=d, q_layer_stride=S * Hq * D, kv_layer_stride=S * Hkv * D,
+                                                out_layer_stride=S * Hq * D, evict=e))
+        dev = batch.device
+        self.streams = [torch.cuda.Stream(device=dev) for _ in self.ranges]
+        self.graphs = []
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        for a in self._args:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for _ in range(self.steps_per_graph):
+                    _lib.call("ic_decode_step", a)
+            self.graphs.append(g)
+        torch.cuda.current_stream(dev).wait_stream(cap)
+
+    @property
+    def launches_per_step(self) -> int:
+        """Kernel launches per step of every session (layers + eviction, per range)."""
+        return self.groups * (self.batch.cfg.num_layers + 1)
+
+    def run(self, replays: int = 1) -> None:
+        cur = torch.cuda.current_stream(self.batch.device)
+        for s in self.streams:
+            s.wait_stream(cur)
+        for _ in range(int(replays)):
+            for s, g in zip(self.streams, self.graphs):
+                with torch.cuda.stream(s):
+                    g.replay()
+        for s in self.streams:
+            cur.wait_stream(s)
 
 
 class HostStepper:

@@ -255,6 +255,61 @@ def test_step_advancing_positions_in_kernel():
         bs[1].step(q[0], k[0], v[0], [1, 2], advance_positions=True)
 
 
+@pytest.mark.parametrize("groups", [1, 2, 3])
+def test_grouped_stepper_matches_steps(groups):
+    """Session ranges on their own streams and graphs (GroupedStepper) give
+    bit-identical outputs and metadata to the same steps of the whole batch."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    S, L, T = 5, 2, 60
+    cfg = CacheConfig(num_layers=L, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=8, important_size=12,
+                      decay=0.99, dtype=torch.float16)
+    g = torch.Generator().manual_seed(31)
+    pk = torch.randn(L, S, 2, T, 128, generator=g).half()
+    pv = torch.randn(L, S, 2, T, 128, generator=g).half()
+    sc = torch.rand(T, generator=g)
+    bs = []
+    for _ in range(2):
+        b = SessionBatch(cfg, S, "cuda:0")
+        for s in range(S):
+            b.load_prompt(s, tuple((pk[l][s][None].cuda(), pv[l][s][None].cuda()) for l in range(L)), sc)
+        bs.append(b)
+    q = torch.randn(L, S, 16, 128, generator=g).half().cuda()
+    k = torch.randn(L, S, 2, 128, generator=g).half().cuda()
+    v = torch.randn(L, S, 2, 128, generator=g).half().cuda()
+    pos0 = torch.arange(T, T + S, dtype=torch.int64, device="cuda")
+    pos1 = pos0.clone()
+    o0 = torch.empty_like(q)
+    o1 = torch.empty_like(q)
+    bs[0].step(q, k, v, pos0, out=o0, advance_positions=True)  # kernels configured before capture
+    bs[1].step(q, k, v, pos1, out=o1, advance_positions=True)
+    st = bs[1].grouped_stepper(q, k, v, o1, pos1, groups=groups, steps_per_graph=2)
+    assert len(st.ranges) == groups and st.launches_per_step == groups * (L + 1)
+    st.run(3)
+    for _ in range(6):
+        bs[0].step(q, k, v, pos0, out=o0, advance_positions=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o0, o1)
+    assert torch.equal(pos0, pos1) and pos1.tolist() == list(range(T + 7, T + 7 + S))
+    for key in ("positions", "importance", "occupied", "slot_table", "ctrl", "counters", "events", "mass"):
+        assert torch.equal(getattr(bs[0], key), getattr(bs[1], key)), key
+
+
+def test_grouped_stepper_rejects_bad_arguments():
+    from infercache_b200 import CacheConfig, SessionBatch
+    cfg = CacheConfig(num_layers=1, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=8, important_size=12,
+                      dtype=torch.float16)
+    b = SessionBatch(cfg, 2, "cuda:0")
+    q = torch.zeros(1, 2, 16, 128, dtype=torch.float16, device="cuda")
+    kv = torch.zeros(1, 2, 2, 128, dtype=torch.float16, device="cuda")
+    pos = torch.zeros(2, dtype=torch.int64, device="cuda")
+    with pytest.raises(ValueError):
+        b.grouped_stepper(q, kv, kv, torch.empty_like(q), pos, groups=3)
+    with pytest.raises(ValueError):
+        b.grouped_stepper(q, kv, kv, torch.empty_like(q), pos.int(), groups=1)
+    with pytest.raises(ValueError):
+        b.grouped_stepper(q.float(), kv, kv, torch.empty_like(q), pos, groups=1)
+
+
 def test_cluster_sizes_agree():
     """8- and 16-CTA clusters differ only in float summation order."""
     from infercache_b200 import CacheConfig, SessionBatch
