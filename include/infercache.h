@@ -376,6 +376,25 @@ typedef struct ic_summary_args {
 } ic_summary_args;
 int ic_summary_score(const ic_summary_args* a, void* stream);
 
+/* ic_summary_score without a caller-provided head_mass buffer (no
+ * counterpart in the reference: an addition of this library).  For callers
+ * that cannot allocate device memory -- code running while another allocator
+ * holds all of the GPU's free memory, or a binding with no CUDA allocator --
+ * the per-head received mass [B, Hq, T] lives in a static device array of
+ * IC_SUMMARY_STATIC_MASS_MAX floats (16 MiB) that the library owns; every GPU
+ * that loads the library holds it until the process exits.  The call
+ * allocates nothing.  Arguments as for ic_summary_score, except: head_mass
+ * must be NULL, colsum is required, and batch * num_q_heads * seq_len must
+ * not exceed IC_SUMMARY_STATIC_MASS_MAX (else IC_ERR_INVALID_ARG).  The first
+ * call on a device looks up the array's device address on the current device
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (other
+ * streams, other host threads) race and corrupt each other's results; order
+ * them on one stream.  No element needs clearing between calls: each call
+ * writes every element it reads. */
+#define IC_SUMMARY_STATIC_MASS_MAX 4194304
+int ic_summary_score_static(const ic_summary_args* a, void* stream);
+
 /* ---- tensor-level helpers with the triton_ops names ---------------------------
  * For callers holding plain K / V buffers and an importance vector (the fused
  * path does not use them). */

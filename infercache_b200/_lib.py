@@ -32,6 +32,7 @@ IC_F32, IC_F16, IC_BF16 = 0, 1, 2
 IC_CTRL_SINK_FILL, IC_CTRL_RECENT_FILL, IC_CTRL_RECENT_PTR, IC_CTRL_IMPORTANT_FILL = 0, 1, 2, 3
 IC_CTRL_WORDS = 8
 IC_CNT_TOKENS_SEEN, IC_CNT_EVICTIONS, IC_CNT_STEPS, IC_CNT_PROMOTIONS = 0, 1, 2, 3
+IC_SUMMARY_STATIC_MASS_MAX = 4194304  # floats of ic_summary_score_static's static scratch
 IC_COUNTER_WORDS = 4
 IC_EV_NONE, IC_EV_DROP, IC_EV_FILL, IC_EV_EVICT, IC_EV_REJECT = 0, 1, 2, 3, 4
 IC_DEVFLAG_TIMEOUT, IC_DEVFLAG_BAD_ROW = 1, 2
@@ -202,6 +203,7 @@ ENTRY_POINTS = {
     "ic_page_gather": ic_page_rows_args,
     "ic_page_write": ic_page_rows_args,
     "ic_summary_score": ic_summary_args,
+    "ic_summary_score_static": ic_summary_args,
     "ic_index_rows": ic_index_rows_args,
     "ic_scatter_mass": ic_scatter_mass_args,
     "ic_argmin_range": ic_argmin_args,

@@ -29,6 +29,8 @@
 #include <cuda.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "exp2_poly.cuh"
 #include "tc05.cuh"
@@ -728,4 +730,83 @@ extern "C" int ic_summary_score(const ic_summary_args* a, void* stream) {
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return a->dtype == IC_BF16 ? ic::launch_summary<__nv_bfloat16>(a, st) : ic::launch_summary<__half>(a, st);
+}
+
+// ------------------------------------------------------------------------------
+// 4. ic_summary_score_static: the scorer with its per-head mass in a library-owned
+//    static device array, for callers that cannot allocate device memory
+// ------------------------------------------------------------------------------
+// Some callers cannot hand this library a scratch buffer: code that runs
+// while another allocator owns all of the GPU's free memory (a serving
+// process that reserved it up front), or a binding from a language with no
+// CUDA allocator at hand.  They still pass q / k / v and every output; the
+// per-head received mass [B, Hq, T], which ic_summary_score takes from the
+// caller, lives here instead.  The array is IC_SUMMARY_STATIC_MASS_MAX floats
+// (16 MiB) and is held by every GPU that loads the library until the process
+// exits.
+namespace {
+
+static __device__ __align__(256) float ic_summary_mass_scratch[IC_SUMMARY_STATIC_MASS_MAX];
+
+constexpr int kScratchMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_addr[kScratchMaxDevices];  // device address of the array, per device
+
+// The array's device address on the current device.  Host code cannot use
+// the array's name as an address (it names a host-side stand-in), so the
+// first call on each device asks the runtime for it, with that device current.
+int scratch_address(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    ic::set_last_error("summary_score_static: cudaGetDevice failed");
+    return IC_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kScratchMaxDevices) {
+    ic::set_last_error("summary_score_static: device index beyond 63");
+    return IC_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, ic_summary_mass_scratch);
+    if (e != cudaSuccess || !p) {
+      ic::set_last_error("summary_score_static: cudaGetSymbolAddress of the static scratch failed");
+      return IC_ERR_CUDA;
+    }
+    g_scratch_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return IC_OK;
+}
+
+}  // namespace
+
+extern "C" int ic_summary_score_static(const ic_summary_args* a, void* stream) {
+  if (!a || !a->q || !a->k || !a->lse || !a->colsum || !a->dev_status) {
+    ic::set_last_error("summary_score_static: null argument (q, k, lse, colsum and dev_status are required)");
+    return IC_ERR_INVALID_ARG;
+  }
+  if (a->head_mass) {
+    ic::set_last_error("summary_score_static: head_mass must be NULL (the per-head mass lives in the static scratch)");
+    return IC_ERR_INVALID_ARG;
+  }
+  if (a->batch < 1 || a->num_q_heads < 1 || a->seq_len < 1) {
+    ic::set_last_error("summary_score_static: bad shape");
+    return IC_ERR_INVALID_ARG;
+  }
+  const long long need = (long long)a->batch * a->num_q_heads * a->seq_len;
+  if (need > (long long)IC_SUMMARY_STATIC_MASS_MAX) {
+    ic::set_last_error("summary_score_static: batch * num_q_heads * seq_len exceeds the static scratch "
+                       "(IC_SUMMARY_STATIC_MASS_MAX floats); use ic_summary_score with a caller buffer");
+    return IC_ERR_INVALID_ARG;
+  }
+  float* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != IC_OK) return rc;
+  // every element of the mass that the column sum reads is written earlier in
+  // the same call, so the array needs no clearing between calls
+  ic_summary_args b = *a;
+  b.head_mass = scratch;
+  return ic_summary_score(&b, stream);
 }
