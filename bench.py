@@ -694,9 +694,10 @@ def main():
                 "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": config_dict(spec, world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": traffic,
-                             "kernel": "decode_lean_kernel (ic_decode_step), one launch = 16 sessions x 1 layer",
+                             "kernel": "decode_lean_kernel (ic_decode_step); unit = one layer of all 16 sessions "
+                                       f"({groups} launches of {S // groups} sessions when grouped)",
                              "alg_bytes_per_launch": alg_bytes, "launch_us": dec_launch_s * 1e6,
-                             "launch_us_basis": "step time / 36 inside the step graph, eviction included",
+                             "launch_us_basis": "step time / 36 inside the step graphs, eviction included",
                              "sequential_attend_us": seq_launch_s * 1e6,
                              "sequential_attend_frac": alg_bytes / seq_launch_s / 1e9 / peak,
                              "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
