@@ -644,29 +644,50 @@ def main():
     # (SessionBatch.host_stepper: one CUDA graph per step, the output copy of
     # step i overlapping step i + 1)
     log("e2e")
-    # q, k and v of a step side by side in one pinned block (one upload per step)
-    block = torch.empty(q.numel() + k.numel() + v.numel(), dtype=q.dtype).pin_memory()
-    qh = block[:q.numel()].view(q.shape)
-    kh = block[q.numel():q.numel() + k.numel()].view(k.shape)
-    vh = block[q.numel() + k.numel():].view(v.shape)
-    qh.copy_(q.cpu())
-    kh.copy_(k.cpu())
-    vh.copy_(v.cpu())
-    ohs = (torch.empty(out.shape, dtype=out.dtype).pin_memory(), torch.empty(out.shape, dtype=out.dtype).pin_memory())
-    stepper = b.host_stepper(qh, kh, vh, ohs, pos)
     ke = max(10, min(args.steps, 500))
-    for _ in range(3):
-        stepper.run()
-    stepper.synchronize()
-    torch.cuda.synchronize()
-    barrier()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record()
-    for _ in range(ke):
-        stepper.run()
-    stepper.synchronize()  # every step's output is on the host before the clock stops
-    x1.record()
-    torch.cuda.synchronize()
+    if groups > 1:
+        # per session range: its q / k / v in one pinned block, uploaded in one
+        # copy, its step, its o downloaded to pinned memory -- one CUDA graph per
+        # range and step, each range on its own stream
+        stepper = b.grouped_host_stepper(pos, num_q_heads=Hq, groups=groups)
+        stepper.load_inputs(q.cpu(), k.cpu(), v.cpu())
+        stepper.run(3)
+        stepper.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        x0.record()
+        stepper.run(ke)  # the current stream waits for every range's last download
+        x1.record()
+        torch.cuda.synchronize()
+        e2e_api = (f"SessionBatch.grouped_host_stepper: per session range ({groups} of {S // groups}), pinned q/k/v "
+                   "block -> device, ic_decode_step, o -> pinned host; one CUDA graph per range and step, each range "
+                   "on its own stream")
+    else:
+        # q, k and v of a step side by side in one pinned block (one upload per step)
+        block = torch.empty(q.numel() + k.numel() + v.numel(), dtype=q.dtype).pin_memory()
+        qh = block[:q.numel()].view(q.shape)
+        kh = block[q.numel():q.numel() + k.numel()].view(k.shape)
+        vh = block[q.numel() + k.numel():].view(v.shape)
+        qh.copy_(q.cpu())
+        kh.copy_(k.cpu())
+        vh.copy_(v.cpu())
+        ohs = (torch.empty(out.shape, dtype=out.dtype).pin_memory(),
+               torch.empty(out.shape, dtype=out.dtype).pin_memory())
+        stepper = b.host_stepper(qh, kh, vh, ohs, pos)
+        for _ in range(3):
+            stepper.run()
+        stepper.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        x0.record()
+        for _ in range(ke):
+            stepper.run()
+        stepper.synchronize()  # every step's output is on the host before the clock stops
+        x1.record()
+        torch.cuda.synchronize()
+        e2e_api = ("SessionBatch.host_stepper: pinned q/k/v (one block) -> device, ic_decode_step, o -> pinned host "
+                   "(one CUDA graph per step; the output copy of step i overlaps step i + 1)")
     barrier()
     e2e_ms = max_over_ranks(x0.elapsed_time(x1))
     e2e_value = world * S * ke / (e2e_ms / 1e3)
@@ -703,8 +724,7 @@ def main():
                              "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                        "steps": ke, "api": "SessionBatch.host_stepper: pinned q/k/v (one block) -> device, ic_decode_step, o -> pinned host "
-                               "(one CUDA graph per step; the output copy of step i overlaps step i + 1)"},
+                        "steps": ke, "api": e2e_api},
                 "gpu_launches": (args.steps // STEPS_PER_GRAPH) * STEPS_PER_GRAPH * groups * (L + 1)
                 + (args.steps % STEPS_PER_GRAPH) * (L + 1),
                 "clocks": sampler.summary() if sampler else None,

@@ -294,6 +294,49 @@ def test_grouped_stepper_matches_steps(groups):
         assert torch.equal(getattr(bs[0], key), getattr(bs[1], key)), key
 
 
+@pytest.mark.parametrize("groups", [1, 3])
+def test_grouped_host_stepper_matches_steps(groups):
+    """Session ranges driven from range-major pinned host buffers on their own
+    streams (GroupedHostStepper) give the outputs and metadata of the same
+    steps run through SessionBatch.step, bit for bit."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    S, L, T = 5, 2, 60
+    cfg = CacheConfig(num_layers=L, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=8, important_size=12,
+                      decay=0.99, dtype=torch.float16)
+    g = torch.Generator().manual_seed(37)
+    pk = torch.randn(L, S, 2, T, 128, generator=g).half()
+    pv = torch.randn(L, S, 2, T, 128, generator=g).half()
+    sc = torch.rand(T, generator=g)
+    bs = []
+    for _ in range(2):
+        b = SessionBatch(cfg, S, "cuda:0")
+        for s in range(S):
+            b.load_prompt(s, tuple((pk[l][s][None].cuda(), pv[l][s][None].cuda()) for l in range(L)), sc)
+        bs.append(b)
+    q = torch.randn(L, S, 16, 128, generator=g).half()
+    k = torch.randn(L, S, 2, 128, generator=g).half()
+    v = torch.randn(L, S, 2, 128, generator=g).half()
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    pos0 = torch.arange(T, T + S, dtype=torch.int64, device="cuda")
+    pos1 = pos0.clone()
+    o0 = torch.empty_like(qd)
+    bs[0].step(qd, kd, vd, pos0, out=o0, advance_positions=True)
+    bs[1].step(qd, kd, vd, pos1, out=torch.empty_like(qd), advance_positions=True)
+    gh = bs[1].grouped_host_stepper(pos1, num_q_heads=16, groups=groups)
+    assert len(gh.ranges) == groups
+    assert gh.h2d_bytes == (q.numel() + k.numel() + v.numel()) * 2 and gh.d2h_bytes == q.numel() * 2
+    gh.load_inputs(q, k, v)
+    gh.run(4)
+    gh.synchronize()
+    for _ in range(4):
+        bs[0].step(qd, kd, vd, pos0, out=o0, advance_positions=True)
+    torch.cuda.synchronize()
+    assert torch.equal(gh.outputs(), o0.cpu())
+    assert torch.equal(pos0, pos1)
+    for key in ("positions", "importance", "occupied", "slot_table", "ctrl", "counters", "events", "mass"):
+        assert torch.equal(getattr(bs[0], key), getattr(bs[1], key)), key
+
+
 def test_grouped_stepper_rejects_bad_arguments():
     from infercache_b200 import CacheConfig, SessionBatch
     cfg = CacheConfig(num_layers=1, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=8, important_size=12,
