@@ -255,7 +255,7 @@ def test_step_advancing_positions_in_kernel():
         bs[1].step(q[0], k[0], v[0], [1, 2], advance_positions=True)
 
 
-@pytest.mark.parametrize("groups", [1, 2, 3])
+@pytest.mark.parametrize("groups", [1, 2, 3, 5])
 def test_grouped_stepper_matches_steps(groups):
     """Session ranges on their own streams and graphs (GroupedStepper) give
     bit-identical outputs and metadata to the same steps of the whole batch."""
@@ -294,7 +294,7 @@ def test_grouped_stepper_matches_steps(groups):
         assert torch.equal(getattr(bs[0], key), getattr(bs[1], key)), key
 
 
-@pytest.mark.parametrize("groups", [1, 3])
+@pytest.mark.parametrize("groups", [1, 3, 5])
 def test_grouped_host_stepper_matches_steps(groups):
     """Session ranges driven from range-major pinned host buffers on their own
     streams (GroupedHostStepper) give the outputs and metadata of the same
