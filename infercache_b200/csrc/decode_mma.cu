@@ -158,6 +158,15 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
     if (!a.inputs_ready) load_inputs();
   }
   if (a.pdl) grid_launch_dependents();
+  // the previous layers' mass sum of this CTA's slots, final once the grid
+  // dependency wait has returned: fetched now so its latency overlaps the scores
+  float* mrow = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + t0;
+  float mprev[MAXT];
+#pragma unroll
+  for (int i = 0; i < MAXT; ++i) {
+    const int t = tid + i * MMA_THREADS;
+    mprev[i] = (a.layer != 0 && t < n) ? mrow[t] : 0.f;
+  }
   for (int i = tid; i < (npad - n) * VPR; i += MMA_THREADS) {
     const int t = n + i / VPR, v = i % VPR;
     reinterpret_cast<int4*>(Ks + t * rowb)[v] = make_int4(0, 0, 0, 0);
@@ -270,13 +279,13 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) decode_mma_kernel(const ic_dec
   __syncthreads();
 
   // -- 4. received mass per slot, summed over the group's heads in order -------
-  {
-    // after this CTA's grid-dependency wait: the previous layer's sum is final
-    float* mrow = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + t0;
-    for (int t = tid; t < n; t += MMA_THREADS) {
+#pragma unroll
+  for (int i = 0; i < MAXT; ++i) {
+    const int t = tid + i * MMA_THREADS;
+    if (t < n) {
       float m = 0.f;
       for (int gg = 0; gg < G; ++gg) m += sc[gg * cp + t];
-      mrow[t] = a.layer == 0 ? m : __fadd_rn(mrow[t], m);
+      mrow[t] = a.layer == 0 ? m : __fadd_rn(mprev[i], m);
     }
   }
 
