@@ -224,6 +224,54 @@ def test_config2_full_size(variant):
     b1.check_device_status()
 
 
+def test_config2_full_size_grouped():
+    """The bench workload at full size (36 layers, 16 sessions, budget 1040,
+    2048-token prompts) stepped as 8 session ranges on their own streams, from
+    device buffers (GroupedStepper) and from host buffers (GroupedHostStepper):
+    outputs and metadata bit-identical to the same steps of the whole batch."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    L, Hq, Hkv, D, S, T = 36, 16, 2, 128, 16, 2048
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=4, recent_size=256,
+                      important_size=780, decay=0.99, dtype=torch.float16)
+    dev = torch.device("cuda", 0)
+
+    def build():
+        gd = torch.Generator(device=dev).manual_seed(5)
+        b = SessionBatch(cfg, S, dev)
+        for s in range(S):
+            pk = torch.randn(L, 1, Hkv, T, D, generator=gd, device=dev).half()
+            pv = torch.randn(L, 1, Hkv, T, D, generator=gd, device=dev).half()
+            b.load_prompt(s, tuple((pk[l], pv[l]) for l in range(L)), torch.rand(T, generator=gd, device=dev))
+        return b
+
+    gd = torch.Generator(device=dev).manual_seed(6)
+    q = torch.randn(L, S, Hq, D, generator=gd, device=dev).half()
+    k = torch.randn(L, S, Hkv, D, generator=gd, device=dev).half()
+    v = torch.randn(L, S, Hkv, D, generator=gd, device=dev).half()
+    bs = [build() for _ in range(3)]
+    pos = [torch.full((S,), T, dtype=torch.int64, device=dev) for _ in range(3)]
+    outs = [torch.empty_like(q) for _ in range(3)]
+    for b, p_, o in zip(bs, pos, outs):
+        b.step(q, k, v, p_, out=o, advance_positions=True)
+    gs = bs[1].grouped_stepper(q, k, v, outs[1], pos[1], groups=8, steps_per_graph=4)
+    gh = bs[2].grouped_host_stepper(pos[2], num_q_heads=Hq, groups=8)
+    gh.load_inputs(q.cpu(), k.cpu(), v.cpu())
+    gs.run(2)
+    gh.run(8)
+    for _ in range(8):
+        bs[0].step(q, k, v, pos[0], out=outs[0], advance_positions=True)
+    gh.synchronize()
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+    assert torch.equal(outs[0].cpu(), gh.outputs())
+    for b in bs[1:]:
+        for key in ("positions", "importance", "occupied", "slot_table", "ctrl", "counters", "events", "mass"):
+            assert torch.equal(getattr(bs[0], key), getattr(b, key)), key
+    assert pos[0].tolist() == [T + 9] * S and torch.equal(pos[0], pos[1]) and torch.equal(pos[0], pos[2])
+    for b in bs:
+        b.check_device_status()
+
+
 def test_step_advancing_positions_in_kernel():
     """advance_positions: kernel B adds one to every session's position after
     reading it; steps driven that way match steps given explicit positions."""
