@@ -10,6 +10,8 @@
 #include <cooperative_groups.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/infercache.h"
 
 namespace ic {
@@ -207,17 +209,60 @@ __device__ __forceinline__ void warp_argmin(float& v, int& i) {
 void set_last_error(const char* msg);
 int launch_status(const char* what);
 
-// Raise a kernel's dynamic shared-memory limit to `bytes` if it is below it
-// (tracked per kernel in `*limit`).  Returns IC_OK or IC_ERR_UNSUPPORTED.
+// Kernel attributes set with cudaFuncSetAttribute apply to the current
+// device's copy of the kernel, so the record of what has been applied is kept
+// per device: a process that drives several GPUs sets each one.  Entries are
+// atomics, so host threads may launch concurrently.
+constexpr int IC_MAX_DEVICES = 64;
+
+inline int current_device_index() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return d;
+}
+
+struct PerDeviceLimit {
+  std::atomic<int> v[IC_MAX_DEVICES];
+};
+
+struct PerDeviceOnce {
+  std::atomic<int> done[IC_MAX_DEVICES];
+};
+
+// Run `fn` once per device (every time on a device index beyond the table).
+template <typename Fn>
+inline void once_per_device(PerDeviceOnce* once, Fn fn) {
+  const int dev = current_device_index();
+  if (dev >= 0 && dev < IC_MAX_DEVICES) {
+    if (once->done[dev].load(std::memory_order_acquire)) return;
+    fn();
+    once->done[dev].store(1, std::memory_order_release);
+    return;
+  }
+  fn();
+}
+
+// Raise a kernel's dynamic shared-memory limit on the current device to
+// `bytes` if it is below it.  Returns IC_OK or IC_ERR_UNSUPPORTED.
 template <typename F>
-inline int ensure_dynamic_smem(F* kernel, int bytes, int* limit) {
-  if (bytes <= 48 * 1024 || bytes <= *limit) return IC_OK;
+inline int ensure_dynamic_smem(F* kernel, int bytes, PerDeviceLimit* limit) {
+  if (bytes <= 48 * 1024) return IC_OK;
+  const int dev = current_device_index();
+  const bool tracked = dev >= 0 && dev < IC_MAX_DEVICES;
+  if (tracked && bytes <= limit->v[dev].load(std::memory_order_acquire)) return IC_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
     cudaGetLastError();
     set_last_error("kernel needs more shared memory than the device allows");
     return IC_ERR_UNSUPPORTED;
   }
-  *limit = bytes;
+  if (tracked) {
+    int cur = limit->v[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !limit->v[dev].compare_exchange_weak(cur, bytes, std::memory_order_acq_rel)) {
+    }
+  }
   return IC_OK;
 }
 

@@ -277,14 +277,13 @@ static int launch_decode(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_UNSUPPORTED;
   }
   auto kern = decode_kernel<T, CL, GP>;
-  static int smem_limit = 0;
+  static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce configured;
+  once_per_device(&configured, [&] {
     if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaGetLastError();
-    configured = true;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.pool.num_kv_heads, a.sess.num_sessions);
   cfg.blockDim = dim3(DEC_THREADS, 1, 1);
@@ -358,15 +357,19 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int variant = a->kernel_variant;
-  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_LEAN) {
+  if (variant < IC_DECODE_AUTO || variant > IC_DECODE_TENSOR_SPLIT) {
     set_last_error("decode: bad kernel_variant");
     return IC_ERR_INVALID_ARG;
   }
   // AUTO on fp16 / bf16: when the step's inputs are all ready (consecutive
   // layers then overlap) the lean kernel (up to 16 query heads per KV head,
-  // else the streaming kernel); one layer at a time, the cluster kernel
-  // (lowest latency for a single launch).
+  // else the streaming kernel); one layer at a time, the slot-split kernel
+  // when the caller gave it a workspace, else the cluster kernel.
   const int G = a->num_q_heads / a->pool.num_kv_heads;
+  if (a->pool.dtype != IC_F32 &&
+      (variant == IC_DECODE_TENSOR_SPLIT ||
+       (variant == IC_DECODE_AUTO && a->workspace && !(a->inputs_ready && a->pdl))))
+    return launch_decode_split(*a, st);
   if (a->pool.dtype != IC_F32 &&
       (variant == IC_DECODE_TENSOR_LEAN || (variant == IC_DECODE_AUTO && a->inputs_ready && a->pdl && G <= 16)))
     return launch_decode_lean(*a, st);

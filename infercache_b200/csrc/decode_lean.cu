@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(W * 32, 8 / W) decode_lean_kernel(const ic_dec
 template <typename T, int NG, int W>
 int launch_one(const ic_decode_args& a, cudaStream_t stream, const LeanSmem& L) {
   auto kern = decode_lean_kernel<T, NG, W>;
-  static int smem_limit = 0;
+  static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.pool.num_kv_heads, a.sess.num_sessions, 1);

@@ -355,14 +355,13 @@ static int launch_mma(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_UNSUPPORTED;
   }
   auto kern = decode_mma_kernel<T, CL, GP>;
-  static int smem_limit = 0;
+  static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
-  static bool configured = false;
-  if (!configured) {
+  static PerDeviceOnce configured;
+  once_per_device(&configured, [&] {
     if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaGetLastError();
-    configured = true;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CL, a.pool.num_kv_heads, a.sess.num_sessions);
   cfg.blockDim = dim3(MMA_THREADS, 1, 1);

@@ -320,7 +320,7 @@ static int launch_stream(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_UNSUPPORTED;
   }
   auto kern = decode_stream_kernel<T, GP>;
-  static int smem_limit = 0;
+  static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.pool.num_kv_heads, a.sess.num_sessions, 1);

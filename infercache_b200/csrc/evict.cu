@@ -366,7 +366,7 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
   // kernel first (the columns are then the bulk of kernel B's reads); the
   // per-session decision kernel starts from the updated importance.
   const bool split = a->mass != nullptr && a->mass_layers >= 8;
-  static int smem_limit_r = 0, smem_limit_f = 0;
+  static PerDeviceLimit smem_limit_r, smem_limit_f;
   int rc = split ? ensure_dynamic_smem(evict_kernel<true>, static_cast<int>(smem), &smem_limit_r)
                  : ensure_dynamic_smem(evict_kernel<false>, static_cast<int>(smem), &smem_limit_f);
   if (rc) return rc;
@@ -403,7 +403,7 @@ extern "C" int ic_sort_slots(const ic_sort_args* a, void* stream) {
   }
   const size_t smem = static_cast<size_t>(a->tiers.budget) * 9;
   if (smem > 200 * 1024) { set_last_error("sort_slots: budget too large"); return IC_ERR_UNSUPPORTED; }
-  static int smem_limit = 0;
+  static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(sort_slots_kernel, static_cast<int>(smem), &smem_limit)) return rc;
   sort_slots_kernel<<<a->sess.num_sessions, SORT_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(*a);
   return launch_status("sort_slots");

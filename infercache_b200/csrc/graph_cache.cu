@@ -366,7 +366,7 @@ extern "C" int ic_graph_push(const ic_graph_push_args* a, void* stream) {
     return IC_ERR_UNSUPPORTED;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  static int lim = 0;
+  static PerDeviceLimit lim;
   if (const int rc = ensure_dynamic_smem(graph_route_kernel, static_cast<int>(smem), &lim)) return rc;
   graph_route_kernel<<<1, GR_THREADS, smem, st>>>(*a);
   if (const int rc = launch_status("graph_push (route)")) return rc;

@@ -671,7 +671,7 @@ int launch_summary(const ic_summary_args* a, cudaStream_t st) {
   p.head_mass = a->head_mass;
   p.status = a->dev_status;
 
-  static int lim_fwd_o = 0, lim_fwd = 0, lim_col = 0;
+  static PerDeviceLimit lim_fwd_o, lim_fwd, lim_col;
   const unsigned grid = (unsigned)(BHq * n_t);
   const unsigned grid_fwd = (unsigned)(BHq * ((n_t + 1) / 2));
   if (a->out) {

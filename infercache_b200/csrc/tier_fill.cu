@@ -207,7 +207,7 @@ extern "C" int ic_tier_fill(const ic_tier_fill_args* a, void* stream) {
   }
   const size_t smem = static_cast<size_t>(t.important_size) * 8;
   if (smem > 200 * 1024) { set_last_error("tier_fill: important_size too large"); return IC_ERR_UNSUPPORTED; }
-  static int smem_limit = 0;
+  static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(tier_fill_kernel, static_cast<int>(smem), &smem_limit)) return rc;
   tier_fill_kernel<<<a->n, 32, smem, static_cast<cudaStream_t>(stream)>>>(*a);
   return launch_status("tier_fill");

@@ -51,7 +51,7 @@ def test_small_protocol(golden, name):
     cache.batch.check_device_status()
 
 
-@pytest.mark.parametrize("variant", [0, 3])
+@pytest.mark.parametrize("variant", [0, 3, 5])
 def test_wide_budget_vs_oracle(variant):
     """Budget 2048 (4/512/1532) with 28/4 heads: the lean kernel then runs
     eight warp pipelines, one CTA per SM (AUTO), and the streaming kernel."""
@@ -60,11 +60,12 @@ def test_wide_budget_vs_oracle(variant):
 
 
 @pytest.mark.parametrize("name", ["f16", "g7"])
-@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5])
 def test_small_protocol_variants(name, variant):
     """Every kernel-A implementation (CUDA cores; tensor cores with one
-    cluster per group; tensor cores streaming a group per CTA) against the
-    oracle."""
+    cluster per group; tensor cores streaming a group per CTA; four warp
+    pipelines per group; CTAs over slot chunks merged by the last to finish)
+    against the oracle."""
     cache, oc, outs, events = run_small(name, variant=variant)
     cache.batch.check_device_status()
 
@@ -164,7 +165,7 @@ def test_batch_sessions_vs_oracle():
     b.check_device_status()
 
 
-@pytest.mark.parametrize("variant", [2, 3, 4])
+@pytest.mark.parametrize("variant", [2, 3, 4, 5])
 def test_config2_full_size(variant):
     """The bench workload at full size: 36 layers, 16 sessions, 16/2 heads,
     budget 4/256/780, fp16, 2048-token prompts.  Session 0 is checked against
@@ -570,4 +571,118 @@ def test_random_small_configs_vs_oracle(i):
     through the fused step: events exact, outputs and importance within the
     dtype's tolerance, every step."""
     cache, oc, outs, events = run_small(_random_spec(i), out_dtype=torch.float32)
+    cache.batch.check_device_status()
+
+
+def _c2_prompts(L, Hkv, D, S, T, seed):
+    g = torch.Generator().manual_seed(seed)
+    return [(torch.randn(L, Hkv, T, D, generator=g).half(), torch.randn(L, Hkv, T, D, generator=g).half(),
+             torch.rand(T, generator=g)) for _ in range(S)], g
+
+
+@pytest.mark.parametrize("split_rows", [0, 64, 128])
+def test_attend_layer_at_a_time_vs_oracle(split_rows):
+    """One layer at a time, as a decoder forward calls it (attend per layer,
+    q of a layer only after the previous layer: no inputs_ready), which runs
+    the slot-split kernel: the bench workload's shapes (36 layers, 16 sessions,
+    16/2 heads, budget 4/256/780, fp16, 2048-token prompts).  Session 0 against
+    the oracle step by step; every session against the cluster kernel (events
+    equal, outputs and importance within 1e-3); a second run reproduces every
+    output bit for bit (the last CTA merges the chunks in chunk order)."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    from infercache_b200 import _lib
+    L, Hq, Hkv, D, S, T, steps = 36, 16, 2, 128, 16, 2048, 4
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=4, recent_size=256,
+                      important_size=780, decay=0.99, dtype=torch.float16)
+    prompts, g = _c2_prompts(L, Hkv, D, S, T, 7)
+    q = torch.randn(steps, L, S, Hq, D, generator=g).half().cuda()
+    k = torch.randn(steps, L, S, Hkv, D, generator=g).half().cuda()
+    v = torch.randn(steps, L, S, Hkv, D, generator=g).half().cuda()
+
+    def build(variant):
+        b = SessionBatch(cfg, S, "cuda:0")
+        b.kernel_variant = variant
+        b.split_rows = split_rows
+        for s in range(S):
+            b.load_prompt(s, tuple((prompts[s][0][l][None].cuda(), prompts[s][1][l][None].cuda())
+                                   for l in range(L)), prompts[s][2])
+        return b
+
+    def run(b, oc=None):
+        outs, evs = [], []
+        for t in range(steps):
+            o = torch.empty(L, S, Hq, D, dtype=torch.float16, device="cuda:0")
+            for l in range(L):
+                b.attend(l, q[t, l], k[t, l], v[t, l], out=o[l])
+            b.evict([T + t] * S)
+            outs.append(o)
+            evs.append(b.events.clone())
+            if oc is not None:
+                oo, e = decode_step(oc, q[t, :, 0].float().cpu().numpy(), k[t, :, 0].float().cpu().numpy(),
+                                    v[t, :, 0].float().cpu().numpy(), T + t, 0.99)
+                assert rows_close(o[:, 0].float().cpu().numpy(), oo, 1e-3), t
+                assert tuple(b.events[0].tolist()) == e.as_tuple(), t
+        return outs, evs
+
+    b1 = build(_lib.IC_DECODE_AUTO)
+    oc = OracleCache(TierGeometry(L, Hkv, D, 4, 256, 780), np.float16)
+    oc.load_from_hf_output(prompts[0][0].float().numpy(), prompts[0][1].float().numpy(), prompts[0][2].numpy())
+    outs1, evs1 = run(b1, oc)
+    assert np.array_equal(b1.positions[0].cpu().numpy(), oc.positions)
+    assert elem_close(b1.importance[0].cpu().numpy(), oc.importance, 1e-3)
+    b1.check_device_status()
+    # the cluster kernel on the same steps
+    b2 = build(_lib.IC_DECODE_TENSOR_CORES)
+    outs2, evs2 = run(b2)
+    for t in range(steps):
+        assert rows_close(outs1[t].float().cpu().numpy(), outs2[t].float().cpu().numpy(), 1e-3), t
+        assert torch.equal(evs1[t], evs2[t]), t
+    assert torch.equal(b1.slot_table, b2.slot_table)
+    assert elem_close(b1.importance.cpu().numpy(), b2.importance.cpu().numpy(), 1e-3)
+    # bit-for-bit reproducible
+    b3 = build(_lib.IC_DECODE_AUTO)
+    outs3, _ = run(b3)
+    for t in range(steps):
+        assert torch.equal(outs1[t], outs3[t]), t
+    assert torch.equal(b1.importance, b3.importance)
+    b3.check_device_status()
+
+
+def run_small_attend(sp, dtype):
+    """run_small with each step taken layer by layer through attend()."""
+    from gpu_protocol import TORCH_DT
+    dt = TORCH_DT[dtype]
+    pk, pv, scores, q, k, v = specs.small_inputs(sp)
+    pk, pv, q, k, v = (t.to(dt).float() for t in (pk, pv, q, k, v))
+    cache = make_gpu_cache(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"], dt,
+                           sp["decay"])
+    oc = OracleCache(TierGeometry(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"]),
+                     np.float32)
+    cache.load_from_hf_output(tuple((pk[l][None].to(dt), pv[l][None].to(dt)) for l in range(sp["layers"])), scores)
+    oc.load_from_hf_output(pk.numpy(), pv.numpy(), scores.numpy())
+    T = pk.shape[2]
+    qd, kd, vd = q.to(dt).cuda(), k.to(dt).cuda(), v.to(dt).cuda()
+    outs, events = [], []
+    for s in range(sp["steps"]):
+        o = torch.stack([cache.attend(l, qd[s, l], kd[s, l], vd[s, l]) for l in range(sp["layers"])])
+        cache.evict(T + s)
+        oo, ev = decode_step(oc, q[s].numpy(), k[s].numpy(), v[s].numpy(), T + s, sp["decay"])
+        g = o.float().cpu().numpy()
+        assert rows_close(g, oo, 1e-3), f"output differs at step {s}: {rows_err(g, oo)}"
+        assert cache.last_event() == ev.as_tuple(), s
+        compare_state(cache, oc, 1e-3, f"step {s}")
+        outs.append(g)
+        events.append(cache.last_event())
+    return cache, oc, np.stack(outs), np.array(events, np.int64)
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+@pytest.mark.parametrize("hq", [8, 32])
+def test_attend_split_kernel_small(dtype, hq):
+    """The slot-split kernel layer at a time on a small primed cache, with 4
+    and 16 query heads per KV head (one and two n = 8 blocks), fp16 and bf16,
+    against the oracle on inputs rounded to the cache dtype."""
+    sp = dict(specs.SMALL["f16"])
+    sp.update(hq=hq, hkv=2)
+    cache, oc, outs, events = run_small_attend(sp, dtype)
     cache.batch.check_device_status()
