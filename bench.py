@@ -482,8 +482,6 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cluster", type=int, default=0)
-    ap.add_argument("--split-rows", type=int, default=0, choices=[0, 64, 128],
-                    help="slots per CTA of the slot-split kernel (one layer at a time); 0 = choose")
     ap.add_argument("--seq-variant", type=int, default=0,
                     help="kernel A variant for the one-layer-at-a-time timing (0 auto: slot-split)")
     ap.add_argument("--no-graph", action="store_true", help="replay steps eagerly instead of as a CUDA graph")
@@ -525,7 +523,6 @@ def main():
     log("priming sessions")
     b = build_batch(spec, device, seed=1234 + rank)
     b.cluster_size = args.cluster
-    b.split_rows = args.split_rows
     g = torch.Generator(device=device).manual_seed(99 + rank)
     q = torch.randn(L, S, Hq, D, generator=g, device=device, dtype=torch.float16)
     k = torch.randn(L, S, Hkv, D, generator=g, device=device, dtype=torch.float16)

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define IC_ABI_VERSION 3
+#define IC_ABI_VERSION 2
 
 /* Status codes.  The Python layer maps them to the reference's exception
  * types: RuntimeError for exhaustion / cap (paged_cache.py:229, 244),
@@ -146,45 +146,28 @@ typedef struct ic_decode_args {
                               come from the immediately preceding kernel */
   float* mass;             /* [S, Hkv, budget + 1] running sum over layers */
   float scale;             /* softmax scale, normally head_dim ** -0.5 */
-  int32_t cluster_size;    /* cluster variant: 0 = choose; else 8 or 16 */
+  int32_t cluster_size;    /* cluster variants: 0 = choose; TENSOR_CORES 8 or
+                              16, TENSOR_SPLIT 1..16 */
   int32_t kernel_variant;  /* ic_decode_variant */
   int32_t pdl;             /* 1: launch with programmatic dependent launch */
-  int32_t split_rows;      /* slot-split variant: slots per CTA, 0 = choose,
-                              else 64 or 128 */
-  int32_t _pad;
-  void* workspace;         /* slot-split variant: device buffer of at least
-                              ic_decode_workspace_bytes() bytes, 256-byte
-                              aligned, zero-filled before its first use (the
-                              kernel leaves it reusable); NULL selects another
-                              variant.  Launches sharing one workspace must be
-                              ordered on one stream. */
-  int64_t workspace_bytes;
 } ic_decode_args;
 
 /* Kernel A implementations.  AUTO picks CUDA cores for fp32 pools; for fp16 /
  * bf16 pools the lean kernel when inputs_ready and pdl are set (the layers of
- * one ic_decode_step overlap); one layer at a time, the slot-split kernel when
- * a workspace is given and the cluster kernel otherwise. */
+ * one ic_decode_step overlap) and the slot-split kernel otherwise (one layer at
+ * a time, as a decoder forward calls it). */
 enum ic_decode_variant {
   IC_DECODE_AUTO = 0,
   IC_DECODE_CUDA_CORES = 1,      /* fp32 / fp16 / bf16, one cluster per group   */
   IC_DECODE_TENSOR_CORES = 2,    /* fp16 / bf16, one cluster per group          */
   IC_DECODE_TENSOR_STREAM = 3,   /* fp16 / bf16, one CTA streams a whole group  */
   IC_DECODE_TENSOR_LEAN = 4,     /* fp16 / bf16, one CTA, four warp pipelines   */
-  IC_DECODE_TENSOR_SPLIT = 5     /* fp16 / bf16, CTAs over chunks of 64 or 128
-                                    slots of every group, partials merged by the
-                                    last CTA to finish (needs `workspace`)      */
+  IC_DECODE_TENSOR_SPLIT = 5     /* fp16 / bf16, a cluster of CTAs over chunks of
+                                    the group's slots, merged through distributed
+                                    shared memory; cluster_size = CTAs per group
+                                    (0 = choose, at most 16)                    */
 };
 int ic_decode_layer(const ic_decode_args* a, void* stream);
-
-/* Bytes of the workspace the slot-split variant needs for these sessions,
- * heads and budget (any split_rows setting); a negative ic_status on bad
- * sizes.  The workspace holds each CTA's partial softmax statistics, its
- * unnormalised output and its chunk's scores, and one arrival counter per
- * (session, KV head).  Same role as the temporaries compact_sdp_attention
- * (triton_ops.py:251-287) allocates per call, here provided once by the
- * caller. */
-int64_t ic_decode_workspace_bytes(const ic_decode_args* a);
 
 /* ---- Kernel B: importance update, promotion / eviction, ring advance -----
  * Once per session-step after the last layer.  For every occupied slot j:

@@ -81,8 +81,7 @@ class ic_decode_args(Structure):
     _fields_ = [("pool", ic_pool), ("tiers", ic_tiers), ("sess", ic_sessions), ("layer", c_int32),
                 ("num_q_heads", c_int32), ("q", c_void_p), ("k_new", c_void_p), ("v_new", c_void_p),
                 ("out", c_void_p), ("out_dtype", c_int32), ("inputs_ready", c_int32), ("mass", c_void_p),
-                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32),
-                ("split_rows", c_int32), ("_pad", c_int32), ("workspace", c_void_p), ("workspace_bytes", c_int64)]
+                ("scale", c_float), ("cluster_size", c_int32), ("kernel_variant", c_int32), ("pdl", c_int32)]
 
 
 class ic_evict_args(Structure):
@@ -215,8 +214,6 @@ ENTRY_POINTS = {
 }
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
 HOST_ENTRY_POINTS = ["ic_host_device_pointer"]
-# host-only size queries: (const args*) -> int64 bytes or a negative status
-SIZE_ENTRY_POINTS = {"ic_decode_workspace_bytes": ic_decode_args}
 
 _LIB = None
 
@@ -244,10 +241,6 @@ def load(path: Path = LIB_PATH):
     lib.ic_last_error.restype = c_char_p
     lib.ic_host_device_pointer.argtypes = [c_void_p, POINTER(c_void_p)]
     lib.ic_host_device_pointer.restype = c_int
-    for name, st in SIZE_ENTRY_POINTS.items():
-        fn = getattr(lib, name)
-        fn.argtypes = [POINTER(st)]
-        fn.restype = c_int64
     _LIB = lib
     return lib
 
@@ -262,15 +255,6 @@ def raise_for(status: int, what: str = "") -> None:
     if status == IC_ERR_UNSUPPORTED:
         raise Unsupported(status, msg)
     raise InferCacheError(status, msg)
-
-
-def size_query(name: str, args) -> int:
-    """A host-only size query (``SIZE_ENTRY_POINTS``): bytes, or raises."""
-    lib = load()
-    n = int(getattr(lib, name)(ctypes.byref(args)))
-    if n < 0:
-        raise_for(n, name)
-    return n
 
 
 def call(name: str, args) -> None:

@@ -363,13 +363,15 @@ extern "C" int ic_decode_layer(const ic_decode_args* a, void* stream) {
   }
   // AUTO on fp16 / bf16: when the step's inputs are all ready (consecutive
   // layers then overlap) the lean kernel (up to 16 query heads per KV head,
-  // else the streaming kernel); one layer at a time, the slot-split kernel
-  // when the caller gave it a workspace, else the cluster kernel.
+  // else the streaming kernel); one layer at a time, the slot-split kernel.
   const int G = a->num_q_heads / a->pool.num_kv_heads;
-  if (a->pool.dtype != IC_F32 &&
-      (variant == IC_DECODE_TENSOR_SPLIT ||
-       (variant == IC_DECODE_AUTO && a->workspace && !(a->inputs_ready && a->pdl))))
-    return launch_decode_split(*a, st);
+  if (a->pool.dtype != IC_F32 && variant == IC_DECODE_TENSOR_SPLIT) return launch_decode_split(*a, st);
+  if (a->pool.dtype != IC_F32 && variant == IC_DECODE_AUTO && !(a->inputs_ready && a->pdl) && G <= 16) {
+    // shapes the slot-split kernel does not cover (budgets beyond 16 CTAs of
+    // 256 slots) fall through to the cluster kernel
+    const int rc = launch_decode_split(*a, st);
+    if (rc != IC_ERR_UNSUPPORTED) return rc;
+  }
   if (a->pool.dtype != IC_F32 &&
       (variant == IC_DECODE_TENSOR_LEAN || (variant == IC_DECODE_AUTO && a->inputs_ready && a->pdl && G <= 16)))
     return launch_decode_lean(*a, st);

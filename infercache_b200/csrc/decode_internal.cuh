@@ -13,8 +13,7 @@ int launch_decode_mma(const ic_decode_args& a, cudaStream_t stream);
 int launch_decode_stream(const ic_decode_args& a, cudaStream_t stream);
 // Tensor-core kernel A, one CTA per group with four independent warp pipelines.
 int launch_decode_lean(const ic_decode_args& a, cudaStream_t stream);
-// Tensor-core kernel A, CTAs over slot chunks, merged by the last CTA (workspace).
+// Tensor-core kernel A, a cluster of CTAs over slot chunks, merged through DSMEM.
 int launch_decode_split(const ic_decode_args& a, cudaStream_t stream);
-int64_t decode_split_workspace_bytes(const ic_decode_args& a);
 
 }  // namespace ic

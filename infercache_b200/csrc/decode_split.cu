@@ -2,31 +2,34 @@
 // sessions, for a decoder that computes each layer's q from the previous
 // layer's output (the layers cannot overlap the way ic_decode_step lets them).
 //
-// The launch fills the machine on its own: the budget + 1 logical slots of
-// every (session, KV head) group are cut into chunks of 64 or 128 slots, one
-// CTA per (chunk, KV head, session) -- at 16 sessions x 2 KV heads x 1041
-// slots, 544 CTAs of four warps.  Per CTA:
-//   1. each warp looks up its 16 or 32 slots in the session's slot table and
-//      issues one 256-byte cp.async.bulk per K row and per V row into padded
-//      shared-memory rows, completing on the warp's own two mbarriers (K, V);
-//      slots past the last are zero rows, the staging slot (the token being
-//      decoded) takes k_new / v_new, which the CTA also writes to the pool.
-//      With programmatic dependent launch, layers after the first issue these
-//      copies before waiting for the previous kernel: the pool rows of this
-//      layer are not written by it;
+// The launch fills the machine on its own: the budget + 1 logical slots of a
+// (session, KV head) group are cut into CL chunks of 16-slot blocks, one CTA
+// per chunk, the group's CTAs one thread-block cluster.  At 16 sessions x 2 KV
+// heads x 1041 slots with CL = 8: 256 CTAs of five warps, 144 slots each.
+// Per CTA:
+//   1. every warp looks up its one or two 16-slot blocks in the session's slot
+//      table and copies their K rows, then their V rows, into padded shared-
+//      memory rows with 16-byte asynchronous copies (two commit groups, so the
+//      scores start as soon as K has landed); slots past the last are zero
+//      rows; the staging slot (the token being decoded) takes k_new / v_new,
+//      which the CTA also writes to the pool.  With programmatic dependent
+//      launch, layers after the first issue these copies before waiting for the
+//      previous kernel: it does not write this layer's pool rows;
 //   2. S^T = K . Q^T on the tensor cores (mma.sync m16n8k16, the warp's K rows
 //      as A through ldmatrix, the group's query heads as B in registers), the
 //      warp's exact per-head maximum, P = 2^(s - max);
 //   3. O^T = V^T . P^T (V rows transposed by ldmatrix.trans, the S^T fragment
 //      turned into the P^T operand by movmatrix.trans);
-//   4. the four warps merge into the CTA's (max, sum, O), which go to the
-//      caller's workspace together with the chunk's log2-scaled scores;
-//   5. the CTA that arrives last for its group (an atomic counter in the
-//      workspace, no waiting) merges the chunks in chunk order -- so the
-//      result does not depend on arrival order -- writes `out`, computes every
-//      slot's received mass from the stored scores with the exact softmax
-//      (summed over the group's heads in head order) and folds it into the
-//      running sum over layers, then resets the counter for the next launch.
+//   4. the warps merge into the CTA's per-head (max, sum, O);
+//   5. the cluster merges without a cluster-wide barrier on the way: every CTA
+//      pushes its (max, sum) pairs into every peer's shared memory with
+//      st.async, completing on the peer's mbarrier; once all CL pairs have
+//      arrived each CTA knows the group's softmax, adds the received mass of
+//      its own slots (summed over the group's heads in head order) to the
+//      running sum over layers, scales its O and pushes slice j of it to CTA j;
+//      CTA j sums the CL slices it receives in CTA order (deterministic) and
+//      writes its part of `out`.
+// No global scratch and no atomics.
 #include <math.h>
 
 #include <type_traits>
@@ -39,41 +42,55 @@ namespace ic {
 namespace {
 
 constexpr int SP_D = 128;
-constexpr int SP_W = 4;                     // warps per CTA
-constexpr int SP_THREADS = SP_W * 32;
+constexpr int SP_MAXW = 8;                  // warps per CTA at most
+constexpr int SP_MAXCL = 16;                // CTAs per cluster at most
 constexpr int SP_PITCH = SP_D * 2 + 16;     // padded row: conflict-free ldmatrix
-constexpr uint32_t SP_ROW_BYTES = SP_D * 2;
-constexpr int SP_MAX_SPLITS = 64;
 constexpr float SP_LOG2E = 1.4426950408889634f;
 
 __host__ __device__ inline int sp_align(int x, int a) { return (x + a - 1) / a * a; }
 
-struct SplitSmem {
-  int k_off, v_off, sc_off, row_off, occ_off, bar_off, flag_off, total, pitch;
+// The geometry of one launch: CL CTAs per group, `chunk` slots per CTA
+// (16-slot blocks), W warps of RB blocks each.
+struct SplitGeom {
+  int cl, chunk, blocks, rb, w, slice;
 };
 
-__host__ __device__ inline SplitSmem split_smem(int chunk, int hs) {
+__host__ __device__ inline SplitGeom split_geometry(int ntot, int hs, int cl_req) {
+  SplitGeom g;
+  // default: 8 CTAs per group (portable cluster size) while they hold at most
+  // 16 blocks of 16 slots each, else as many as 16-block CTAs need
+  const int cl0 = cl_req > 0 ? cl_req : (ntot <= 8 * 256 ? 8 : (ntot + 255) / 256);
+  g.blocks = (ntot + 16 * cl0 - 1) / (16 * cl0);
+  g.chunk = 16 * g.blocks;
+  g.cl = (ntot + g.chunk - 1) / g.chunk;
+  g.rb = g.blocks > SP_MAXW ? 2 : 1;
+  g.w = (g.blocks + g.rb - 1) / g.rb;
+  g.slice = sp_align((hs * SP_D + g.cl - 1) / g.cl, 4);  // O floats reduced by each CTA
+  return g;
+}
+
+struct SplitSmem {
+  int k_off, v_off, sc_off, row_off, occ_off, stin_off, red_off, ocs_off, cst_off, bar_off, total, pitch, rows;
+};
+
+__host__ __device__ inline SplitSmem split_smem(const SplitGeom& g, int hs) {
   SplitSmem L;
+  L.rows = 16 * g.rb * g.w;  // rows the warps cover (>= chunk)
   int o = 0;
-  L.k_off = o;   o += chunk * SP_PITCH;
-  L.v_off = o;   o += chunk * SP_PITCH;
-  L.pitch = chunk + 4;
-  L.sc_off = o;  o += hs * L.pitch * 4;
-  L.row_off = o; o += chunk * 4;
-  L.occ_off = o; o = sp_align(o + chunk, 16);
-  L.bar_off = o; o += 2 * SP_W * 8;
-  L.flag_off = o; o += 16;
+  L.k_off = o;    o += L.rows * SP_PITCH;
+  L.v_off = o;    o += L.rows * SP_PITCH;
+  L.pitch = L.rows + 4;
+  L.sc_off = o;   o += hs * L.pitch * 4;
+  L.row_off = o;  o += L.rows * 4;
+  L.occ_off = o;  o = sp_align(o + L.rows, 16);
+  L.stin_off = o; o += SP_MAXCL * hs * 2 * 4;        // [CL][hs] (max, sum) from every CTA
+  L.red_off = o;  o += g.cl * g.slice * 4;           // [CL][slice] O slices from every CTA
+  L.ocs_off = o;  o += hs * SP_D * 4;                // this CTA's merged O [hs][128]
+  L.cst_off = o;  o += 4 * hs * 4;                   // m_cta, l_cta, M, 1 / L per head
+  L.bar_off = o;  o += 16;                           // mbarriers: stats, O slices
   L.total = o;
   return L;
 }
-
-// Floats of one (session, KV head) group's workspace: per chunk the CTA's
-// per-head max and sum, its unnormalised O [hs][128] and the chunk's
-// log2-scaled scores [chunk][hs].
-__host__ __device__ inline size_t split_group_floats(int splits, int chunk, int hs) {
-  return static_cast<size_t>(splits) * hs * (2 + SP_D + chunk);
-}
-__host__ __device__ inline size_t split_counter_bytes(size_t groups) { return (groups * 4 + 255) / 256 * 256; }
 
 __device__ __forceinline__ uint32_t sp_movtrans(uint32_t x) {
   uint32_t y;
@@ -92,33 +109,71 @@ __device__ __forceinline__ float sp_ex2(float x) {
   return y;
 }
 
+// Wait for an mbarrier phase completed by other CTAs' st.async (cluster-scope
+// acquire), bounded like mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, int32_t* status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_timer_ns() - t0 > 2000000000ull) {
+      if (status) atomicOr(status, IC_DEVFLAG_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 template <typename T, int NG, int RB>
-__global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_decode_args a, int splits) {
+__global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_decode_args a, SplitGeom geo) {
   constexpr int HS = NG * 8;        // query heads per group, padded to the mma's n = 8
   constexpr int R = 16 * RB;        // slots per warp
-  constexpr int CHUNK = SP_W * R;   // slots per CTA
   constexpr bool SPLITP = std::is_same<T, __nv_bfloat16>::value;  // P as high + low bf16
   extern __shared__ __align__(128) unsigned char smem[];
-  const int c = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int c = static_cast<int>(cluster_ctarank());
+  const int h = blockIdx.y, s = blockIdx.z;
+  const int nthr = blockDim.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tq = lane & 3;
   const int budget = a.tiers.budget, ntot = budget + 1;
   const int Hkv = a.pool.num_kv_heads, Hq = a.num_q_heads, G = Hq / Hkv;
-  const SplitSmem L = split_smem(CHUNK, HS);
+  const int CL = geo.cl, chunk = geo.chunk, W = geo.w, SL = geo.slice;
+  const SplitSmem L = split_smem(geo, HS);
   unsigned char* Ks = smem + L.k_off;
   unsigned char* Vs = smem + L.v_off;
   float* sc = reinterpret_cast<float*>(smem + L.sc_off);  // [HS][pitch] log2-scaled scores
   int32_t* rows = reinterpret_cast<int32_t*>(smem + L.row_off);
   uint8_t* occ_s = smem + L.occ_off;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // [warp][K, V]
-  int* flag = reinterpret_cast<int*>(smem + L.flag_off);
+  float* stin = reinterpret_cast<float*>(smem + L.stin_off);   // [CL][HS][2]
+  float* red = reinterpret_cast<float*>(smem + L.red_off);     // [CL][SL]
+  float* ocs = reinterpret_cast<float*>(smem + L.ocs_off);     // [HS][SP_D]
+  float* cst = reinterpret_cast<float*>(smem + L.cst_off);     // [4][HS]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   const int pitch = L.pitch;
+  const int own0 = c * chunk;                      // first slot of this CTA
+  const int nown = max(0, min(chunk, ntot - own0));  // slots it owns
+  const int red_len = max(0, min(SL, HS * SP_D - c * SL));  // O floats it reduces
 
   if (tid == 0) {
-    for (int i = 0; i < 2 * SP_W; ++i) mbar_init(&bar[i], 1);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_barrier_init();
+    mbar_arrive_expect_tx(&bar[0], static_cast<uint32_t>(CL * HS * 2 * 4));
+    mbar_arrive_expect_tx(&bar[1], static_cast<uint32_t>(CL * red_len * 4));
   }
-  __syncthreads();
+  // peers may push into this CTA's shared memory once every CTA has passed here
+  cluster_arrive_release();
 
   // Layer 0 may follow the eviction kernel, which rewrites the slot table and
   // occupancy: wait first.  Later layers read nothing the previous kernel
@@ -133,50 +188,50 @@ __global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_de
   const int32_t* st = a.sess.slot_table + static_cast<size_t>(s) * ntot;
   const uint8_t* occ_g = a.sess.occupied + static_cast<size_t>(s) * budget;
 
-  // ---- 1. this warp's rows: slot table, then one bulk copy per K and V row ------
+  // ---- 1. this warp's rows: slot table, then 16-byte asynchronous copies -------
   const int wbase = warp * R;              // first row of this warp in the CTA
-  const int t0 = c * CHUNK + wbase;        // its first logical slot
-  uint64_t* kbar = &bar[2 * warp];
-  uint64_t* vbar = &bar[2 * warp + 1];
-  int my_row = -1;                         // pool row; -2 staging slot; -1 past the last slot
-  bool my_copy = false;
   if (lane < R) {
-    const int t = t0 + lane;
+    const int r = wbase + lane;
+    const int t = own0 + r;
+    int row = -1;                          // pool row; -2 staging slot; -1 no slot
     uint8_t o = 0;
-    if (t < budget) {
-      my_row = st[t];
-      o = occ_g[t];
-      if (static_cast<unsigned long long>(my_row) >= static_cast<unsigned long long>(a.pool.pool_tokens)) {
-        if (a.sess.dev_status) atomicOr(a.sess.dev_status, IC_DEVFLAG_BAD_ROW);
-        my_row = 0;
-        o = 0;
+    if (r < nown) {
+      if (t < budget) {
+        row = st[t];
+        o = occ_g[t];
+        if (static_cast<unsigned long long>(row) >= static_cast<unsigned long long>(a.pool.pool_tokens)) {
+          if (a.sess.dev_status) atomicOr(a.sess.dev_status, IC_DEVFLAG_BAD_ROW);
+          row = 0;
+          o = 0;
+        }
+      } else {
+        row = -2;
+        o = 1;
       }
-      my_copy = true;
-    } else if (t == budget) {
-      my_row = -2;
-      o = 1;
     }
-    rows[wbase + lane] = my_row;
-    occ_s[wbase + lane] = o;
-  }
-  const uint32_t ncopy = __popc(__ballot_sync(FULL_MASK, my_copy));
-  if (lane == 0) {
-    mbar_arrive_expect_tx(kbar, ncopy * SP_ROW_BYTES);
-    mbar_arrive_expect_tx(vbar, ncopy * SP_ROW_BYTES);
+    rows[r] = row;
+    occ_s[r] = o;
   }
   __syncwarp();
-  if (my_copy) {
-    bulk_g2s(Ks + (wbase + lane) * SP_PITCH, pk + static_cast<size_t>(my_row) * SP_D, SP_ROW_BYTES, kbar);
-    bulk_g2s(Vs + (wbase + lane) * SP_PITCH, pv + static_cast<size_t>(my_row) * SP_D, SP_ROW_BYTES, vbar);
-  }
-  // rows past the last slot are zero (their scores are masked; V must be finite)
+  // K rows in one commit group, V rows in a second; half-warps take a row per
+  // pass (256 contiguous bytes); rows without a slot are zero (their scores are
+  // masked; V must be finite)
   constexpr int VPR = SP_D * 2 / 16;  // 16-byte vectors per row
-  for (int i = lane; i < R * VPR; i += 32) {
-    const int r = i / VPR, v = i % VPR;
-    if (rows[wbase + r] == -1) {
-      reinterpret_cast<int4*>(Ks + (wbase + r) * SP_PITCH)[v] = make_int4(0, 0, 0, 0);
-      reinterpret_cast<int4*>(Vs + (wbase + r) * SP_PITCH)[v] = make_int4(0, 0, 0, 0);
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    unsigned char* dst = pass == 0 ? Ks : Vs;
+    const T* src = pass == 0 ? pk : pv;
+#pragma unroll 4
+    for (int i = lane; i < R * VPR; i += 32) {
+      const int r = wbase + i / VPR, v = i % VPR;
+      const int row = rows[r];
+      unsigned char* d = dst + r * SP_PITCH + v * 16;
+      if (row >= 0)
+        cp_async16(d, src + static_cast<size_t>(row) * SP_D + v * 8);
+      else if (row == -1)
+        *reinterpret_cast<int4*>(d) = make_int4(0, 0, 0, 0);
     }
+    cp_async_commit();
   }
 
   if (early) grid_dependency_wait();
@@ -199,15 +254,15 @@ __global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_de
     }
   }
   // the staging slot: the new token's K/V into shared memory and the pool
-  if (t0 <= budget && budget < t0 + R) {
-    const int r = budget - t0;
+  if (own0 + wbase <= budget && budget < own0 + wbase + R && budget - own0 < nown) {
+    const int r = budget - own0;
     const T* kn = static_cast<const T*>(a.k_new) + (static_cast<size_t>(s) * Hkv + h) * SP_D;
     const T* vn = static_cast<const T*>(a.v_new) + (static_cast<size_t>(s) * Hkv + h) * SP_D;
     if (lane < VPR) {
       const int4 kv = reinterpret_cast<const int4*>(kn)[lane];
       const int4 vv = reinterpret_cast<const int4*>(vn)[lane];
-      reinterpret_cast<int4*>(Ks + (wbase + r) * SP_PITCH)[lane] = kv;
-      reinterpret_cast<int4*>(Vs + (wbase + r) * SP_PITCH)[lane] = vv;
+      reinterpret_cast<int4*>(Ks + r * SP_PITCH)[lane] = kv;
+      reinterpret_cast<int4*>(Vs + r * SP_PITCH)[lane] = vv;
       const int row = st[budget];
       if (static_cast<unsigned long long>(row) < static_cast<unsigned long long>(a.pool.pool_tokens)) {
         reinterpret_cast<int4*>(static_cast<T*>(a.pool.k) + lh * plane + static_cast<size_t>(row) * SP_D)[lane] = kv;
@@ -217,11 +272,20 @@ __global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_de
       }
     }
   }
-  __syncwarp();
+  // the previous layers' mass sum of this CTA's slots (final once the grid
+  // dependency wait has returned), fetched now so its latency overlaps the scores
+  float* macc = a.mass + (static_cast<size_t>(s) * Hkv + h) * ntot + own0;
+  float mprev[2] = {0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = tid + i * nthr;
+    if (a.layer > 0 && r < nown) mprev[i] = macc[r];
+  }
 
   // ---- 2. S^T = K Q^T, the warp's per-head max, P ---------------------------------
   const float sl2 = a.scale * SP_LOG2E;
-  const bool k_ok = mbar_wait_bounded(kbar, 0, a.sess.dev_status);
+  cp_async_wait<1>();
+  __syncwarp();
   float acc[RB][NG][4];
 #pragma unroll
   for (int rb = 0; rb < RB; ++rb) {
@@ -303,7 +367,8 @@ __global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_de
       for (int off = 4; off < 32; off <<= 1) lw[nt][j] += __shfl_xor_sync(FULL_MASK, lw[nt][j], off);
 
   // ---- 3. O^T = V^T P^T -------------------------------------------------------------
-  const bool v_ok = mbar_wait_bounded(vbar, 0, a.sess.dev_status);
+  cp_async_wait<0>();
+  __syncwarp();
   float o[NG][8][4];
 #pragma unroll
   for (int nt = 0; nt < NG; ++nt)
@@ -324,15 +389,12 @@ __global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_de
       }
     }
   }
-  // a copy that outlived its bounded wait must land before the CTA leaves
-  if (!k_ok) mbar_wait_bounded(kbar, 0, a.sess.dev_status);
-  if (!v_ok) mbar_wait_bounded(vbar, 0, a.sess.dev_status);
 
-  // ---- 4. merge the warps; the CTA's partial to the workspace -----------------------
-  __syncthreads();  // K / V rows are free: the merge buffers alias them
-  float* wo = reinterpret_cast<float*>(smem);  // [warp][HS][SP_D]
-  float* wm = wo + SP_W * HS * SP_D;           // [warp][HS]
-  float* wl = wm + SP_W * HS;                  // [warp][HS]
+  // ---- 4. merge the warps into the CTA's (max, sum, O) ------------------------------
+  __syncthreads();  // K / V rows are free: the warp buffers alias them
+  float* wo = reinterpret_cast<float*>(smem);  // [W][HS][SP_D]
+  float* wm = wo + W * HS * SP_D;              // [W][HS]
+  float* wl = wm + W * HS;                     // [W][HS]
 #pragma unroll
   for (int nt = 0; nt < NG; ++nt) {
 #pragma unroll
@@ -351,227 +413,147 @@ __global__ void __launch_bounds__(SP_THREADS, 4) decode_split_kernel(const ic_de
     }
   }
   __syncthreads();
-  const size_t groups = static_cast<size_t>(a.sess.num_sessions) * Hkv;
-  const size_t grp = static_cast<size_t>(s) * Hkv + h;
-  int* counter = static_cast<int*>(a.workspace) + grp;
-  float* ws = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + split_counter_bytes(groups)) +
-              grp * split_group_floats(splits, CHUNK, HS);
-  float* ws_m = ws;                                     // [splits][HS]
-  float* ws_l = ws_m + splits * HS;                     // [splits][HS]
-  float* ws_o = ws_l + splits * HS;                     // [splits][HS][SP_D]
-  float* ws_x = ws_o + static_cast<size_t>(splits) * HS * SP_D;  // [splits * CHUNK][HS]
-  for (int e = tid; e < HS * (SP_D / 8); e += SP_THREADS) {
-    const int head = e / (SP_D / 8), d0 = (e % (SP_D / 8)) * 8;
+  float* m_cta = cst;
+  float* l_cta = cst + HS;
+  float* gM = cst + 2 * HS;
+  float* gI = cst + 3 * HS;
+  for (int e = tid; e < HS * (SP_D / 4); e += nthr) {
+    const int head = e / (SP_D / 4), d0 = (e % (SP_D / 4)) * 4;
     float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < SP_W; ++w) M = fmaxf(M, wm[w * HS + head]);
-    float f[SP_W], lsum = 0.f;
-#pragma unroll
-    for (int w = 0; w < SP_W; ++w) {
+    for (int w = 0; w < W; ++w) M = fmaxf(M, wm[w * HS + head]);
+    float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f, lsum = 0.f;
+    for (int w = 0; w < W; ++w) {
       const float m = wm[w * HS + head];
-      f[w] = m == -INFINITY ? 0.f : sp_ex2(m - M);
-      lsum = fmaf(wl[w * HS + head], f[w], lsum);
+      const float f = m == -INFINITY ? 0.f : sp_ex2(m - M);
+      lsum = fmaf(wl[w * HS + head], f, lsum);
+      const float4 u = *reinterpret_cast<const float4*>(wo + (w * HS + head) * SP_D + d0);
+      x0 = fmaf(u.x, f, x0); x1 = fmaf(u.y, f, x1); x2 = fmaf(u.z, f, x2); x3 = fmaf(u.w, f, x3);
     }
-    float x[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      x[i] = 0.f;
-#pragma unroll
-      for (int w = 0; w < SP_W; ++w) x[i] = fmaf(wo[(w * HS + head) * SP_D + d0 + i], f[w], x[i]);
-    }
-    float4* dst = reinterpret_cast<float4*>(ws_o + (static_cast<size_t>(c) * HS + head) * SP_D + d0);
-    __stcg(dst, make_float4(x[0], x[1], x[2], x[3]));
-    __stcg(dst + 1, make_float4(x[4], x[5], x[6], x[7]));
+    *reinterpret_cast<float4*>(ocs + head * SP_D + d0) = make_float4(x0, x1, x2, x3);
     if (d0 == 0) {
-      __stcg(ws_m + c * HS + head, M);
-      __stcg(ws_l + c * HS + head, lsum);
+      m_cta[head] = M;
+      l_cta[head] = lsum;
     }
   }
-  for (int t = tid; t < CHUNK; t += SP_THREADS) {
-    float4* dst = reinterpret_cast<float4*>(ws_x + (static_cast<size_t>(c) * CHUNK + t) * HS);
-#pragma unroll
-    for (int q4 = 0; q4 < HS / 4; ++q4)
-      __stcg(dst + q4, make_float4(sc[(4 * q4) * pitch + t], sc[(4 * q4 + 1) * pitch + t],
-                                   sc[(4 * q4 + 2) * pitch + t], sc[(4 * q4 + 3) * pitch + t]));
-  }
-  __threadfence();
   __syncthreads();
-  if (tid == 0) flag[0] = atomicAdd(counter, 1) == splits - 1;
-  __syncthreads();
-  if (!flag[0]) return;
 
-  // ---- 5. the last CTA of the group: merge the chunks in order ------------------------
-  __threadfence();
-  float* fcs = reinterpret_cast<float*>(smem);   // [splits][HS] chunk weights, then / L
-  float* fls = fcs + SP_MAX_SPLITS * HS;         // [splits][HS] chunk sums
-  float* gM = fls + SP_MAX_SPLITS * HS;          // [HS] global max
-  float* gI = gM + HS;                           // [HS] 1 / global sum
-  for (int i = tid; i < splits * HS; i += SP_THREADS) {
-    fcs[i] = __ldcg(ws_m + i);
-    fls[i] = __ldcg(ws_l + i);
+  // ---- 5. cluster merge --------------------------------------------------------------
+  cluster_wait_acquire();  // every peer has initialised its mbarriers
+  if (tid < HS) {
+    const uint32_t src = smem_addr(stin + (c * HS + tid) * 2);
+    const uint32_t b0 = smem_addr(&bar[0]);
+    const uint32_t mx = __float_as_uint(m_cta[tid]), ls = __float_as_uint(l_cta[tid]);
+    for (int j = 0; j < CL; ++j) st_async_v2(map_shared(src, j), mx, ls, map_shared(b0, j));
   }
-  __syncthreads();
+  mbar_wait_cluster_bounded(&bar[0], 0, a.sess.dev_status);
   if (tid < HS) {
     float M = -INFINITY;
-    for (int k = 0; k < splits; ++k) M = fmaxf(M, fcs[k * HS + tid]);
+    for (int j = 0; j < CL; ++j) M = fmaxf(M, stin[(j * HS + tid) * 2]);
     float lsum = 0.f;
-    for (int k = 0; k < splits; ++k) {
-      const float m = fcs[k * HS + tid];
-      const float f = m == -INFINITY ? 0.f : sp_ex2(m - M);
-      fcs[k * HS + tid] = f;
-      lsum = fmaf(fls[k * HS + tid], f, lsum);
+    for (int j = 0; j < CL; ++j) {
+      const float m = stin[(j * HS + tid) * 2];
+      lsum = fmaf(stin[(j * HS + tid) * 2 + 1], m == -INFINITY ? 0.f : sp_ex2(m - M), lsum);
     }
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     gM[tid] = M;
-    gI[tid] = inv;
-    for (int k = 0; k < splits; ++k) fcs[k * HS + tid] *= inv;
+    gI[tid] = lsum > 0.f ? 1.f / lsum : 0.f;
   }
   __syncthreads();
+  // received mass of this CTA's slots (exact softmax, heads in order), folded into
+  // the running sum over layers after the previous layer's kernel has completed
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = tid + i * nthr;
+    if (r < nown) {
+      float m = 0.f;
+      for (int head = 0; head < G; ++head) {
+        const float x = sc[head * pitch + r];
+        if (x != -INFINITY) m += sp_ex2(x - gM[head]) * gI[head];
+      }
+      macc[r] = a.layer == 0 ? m : __fadd_rn(mprev[i], m);
+    }
+  }
+  for (int r = tid + 2 * nthr; r < nown; r += nthr) {  // chunks longer than two rows per thread
+    float m = 0.f;
+    for (int head = 0; head < G; ++head) {
+      const float x = sc[head * pitch + r];
+      if (x != -INFINITY) m += sp_ex2(x - gM[head]) * gI[head];
+    }
+    macc[r] = a.layer == 0 ? m : __fadd_rn(macc[r], m);
+  }
+  // this CTA's O scaled to the group's softmax, slice j pushed to CTA j
+  {
+    const uint32_t b1 = smem_addr(&bar[1]);
+    for (int e4 = tid; e4 < HS * SP_D / 4; e4 += nthr) {
+      const int e = 4 * e4, head = e / SP_D;
+      const float m = m_cta[head];
+      const float f = m == -INFINITY ? 0.f : sp_ex2(m - gM[head]) * gI[head];
+      const float4 u = *reinterpret_cast<const float4*>(ocs + e);
+      const int j = e / SL, off = e - j * SL;
+      const uint32_t dst = map_shared(smem_addr(red + c * SL + off), j);
+      st_async_v4(dst, __float_as_uint(u.x * f), __float_as_uint(u.y * f), __float_as_uint(u.z * f),
+                  __float_as_uint(u.w * f), map_shared(b1, j));
+    }
+  }
+  mbar_wait_cluster_bounded(&bar[1], 0, a.sess.dev_status);
+  // sum the CL slices of this CTA's part of O in CTA order; heads past G are padding
   {
     const size_t ob = (static_cast<size_t>(s) * Hq + static_cast<size_t>(h) * G) * SP_D;
-    for (int e = tid; e < G * (SP_D / 8); e += SP_THREADS) {
-      const int head = e / (SP_D / 8), d0 = (e % (SP_D / 8)) * 8;
-      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      const float4* src = reinterpret_cast<const float4*>(ws_o + static_cast<size_t>(head) * SP_D + d0);
-      constexpr size_t CSTRIDE = static_cast<size_t>(HS) * SP_D / 4;  // float4s per chunk
-      int k = 0;
-      for (; k + 4 <= splits; k += 4) {  // four chunks' loads in flight
-        float4 u[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          u[i][0] = __ldcg(src + (k + i) * CSTRIDE);
-          u[i][1] = __ldcg(src + (k + i) * CSTRIDE + 1);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float f = fcs[(k + i) * HS + head];
-          x[0] = fmaf(u[i][0].x, f, x[0]); x[1] = fmaf(u[i][0].y, f, x[1]);
-          x[2] = fmaf(u[i][0].z, f, x[2]); x[3] = fmaf(u[i][0].w, f, x[3]);
-          x[4] = fmaf(u[i][1].x, f, x[4]); x[5] = fmaf(u[i][1].y, f, x[5]);
-          x[6] = fmaf(u[i][1].z, f, x[6]); x[7] = fmaf(u[i][1].w, f, x[7]);
-        }
+    for (int e4 = tid; e4 < red_len / 4; e4 += nthr) {
+      const int e = c * SL + 4 * e4, head = e / SP_D;
+      if (head >= G) continue;
+      float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+      for (int j = 0; j < CL; ++j) {
+        const float4 u = *reinterpret_cast<const float4*>(red + j * SL + 4 * e4);
+        x0 += u.x; x1 += u.y; x2 += u.z; x3 += u.w;
       }
-      for (; k < splits; ++k) {
-        const float4 u0 = __ldcg(src + k * CSTRIDE), u1 = __ldcg(src + k * CSTRIDE + 1);
-        const float f = fcs[k * HS + head];
-        x[0] = fmaf(u0.x, f, x[0]); x[1] = fmaf(u0.y, f, x[1]);
-        x[2] = fmaf(u0.z, f, x[2]); x[3] = fmaf(u0.w, f, x[3]);
-        x[4] = fmaf(u1.x, f, x[4]); x[5] = fmaf(u1.y, f, x[5]);
-        x[6] = fmaf(u1.z, f, x[6]); x[7] = fmaf(u1.w, f, x[7]);
-      }
-      const size_t o0 = ob + static_cast<size_t>(head) * SP_D + d0;
+      const size_t o0 = ob + e;
       if (a.out_dtype == IC_F32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + o0);
-        dst[0] = make_float4(x[0], x[1], x[2], x[3]);
-        dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+        *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o0) = make_float4(x0, x1, x2, x3);
       } else {
-        *reinterpret_cast<uint4*>(static_cast<T*>(a.out) + o0) =
-            make_uint4(sp_pack<T>(x[0], x[1]), sp_pack<T>(x[2], x[3]), sp_pack<T>(x[4], x[5]),
-                       sp_pack<T>(x[6], x[7]));
+        *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + o0) = make_uint2(sp_pack<T>(x0, x1), sp_pack<T>(x2, x3));
       }
     }
   }
-  // received mass of every slot (exact softmax, heads in order), folded into
-  // the running sum over layers: the previous layer completed before the
-  // grid-dependency wait returned
-  float* macc = a.mass + grp * ntot;
-  for (int tb = 0; tb < ntot; tb += 4 * SP_THREADS) {
-    float xs[4][HS];
-    float prev[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = tb + i * SP_THREADS + tid;
-      const bool in = t < ntot;
-      const float4* src = reinterpret_cast<const float4*>(ws_x + static_cast<size_t>(in ? t : 0) * HS);
-#pragma unroll
-      for (int q4 = 0; q4 < HS / 4; ++q4) {
-        const float4 u = __ldcg(src + q4);
-        xs[i][4 * q4] = u.x; xs[i][4 * q4 + 1] = u.y; xs[i][4 * q4 + 2] = u.z; xs[i][4 * q4 + 3] = u.w;
-      }
-      prev[i] = (a.layer > 0 && in) ? macc[t] : 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = tb + i * SP_THREADS + tid;
-      if (t >= ntot) continue;
-      float m = 0.f;
-#pragma unroll
-      for (int head = 0; head < HS; ++head) {
-        const float xv = xs[i][head];
-        if (head < G && xv != -INFINITY) m += sp_ex2(xv - gM[head]) * gI[head];
-      }
-      macc[t] = a.layer == 0 ? m : __fadd_rn(prev[i], m);
-    }
-  }
-  if (tid == 0) *counter = 0;  // ready for the next launch
-}
-
-struct SplitGeom {
-  int rb, chunk, splits, hs;
-};
-
-inline SplitGeom split_geometry(int ntot, int G, int split_rows) {
-  SplitGeom g;
-  g.hs = G <= 8 ? 8 : 16;
-  if (split_rows == 64 || split_rows == 128) {
-    g.chunk = split_rows;
-  } else {
-    g.chunk = (ntot + 63) / 64 <= SP_MAX_SPLITS ? 64 : 128;
-  }
-  g.rb = g.chunk / (16 * SP_W);
-  g.splits = (ntot + g.chunk - 1) / g.chunk;
-  return g;
-}
-
-inline size_t split_workspace_bytes(int num_sessions, int Hkv, const SplitGeom& g) {
-  const size_t groups = static_cast<size_t>(num_sessions) * Hkv;
-  return split_counter_bytes(groups) + groups * split_group_floats(g.splits, g.chunk, g.hs) * 4;
 }
 
 template <typename T, int NG, int RB>
-int launch_split(const ic_decode_args& a, cudaStream_t stream, int splits) {
-  constexpr int CHUNK = SP_W * 16 * RB;
-  const SplitSmem L = split_smem(CHUNK, NG * 8);
+int launch_split(const ic_decode_args& a, cudaStream_t stream, const SplitGeom& geo) {
+  const SplitSmem L = split_smem(geo, NG * 8);
   auto kern = decode_split_kernel<T, NG, RB>;
   static PerDeviceLimit smem_limit;
   if (const int rc = ensure_dynamic_smem(kern, L.total, &smem_limit)) return rc;
+  if (geo.cl > 8) {
+    static PerDeviceOnce nonportable;
+    once_per_device(&nonportable, [&] {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      cudaGetLastError();
+    });
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(splits, a.pool.num_kv_heads, a.sess.num_sessions);
-  cfg.blockDim = dim3(SP_THREADS, 1, 1);
+  cfg.gridDim = dim3(geo.cl, a.pool.num_kv_heads, a.sess.num_sessions);
+  cfg.blockDim = dim3(32 * geo.w, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = geo.cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, kern, a, splits);
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, kern, a, geo);
   return launch_status("decode_layer (split)");
 }
 
 template <typename T>
-int split_dispatch(const ic_decode_args& a, cudaStream_t stream, const SplitGeom& g) {
-  if (g.hs == 8)
-    return g.rb == 1 ? launch_split<T, 1, 1>(a, stream, g.splits) : launch_split<T, 1, 2>(a, stream, g.splits);
-  return g.rb == 1 ? launch_split<T, 2, 1>(a, stream, g.splits) : launch_split<T, 2, 2>(a, stream, g.splits);
+int split_dispatch(const ic_decode_args& a, cudaStream_t stream, const SplitGeom& g, int hs) {
+  if (hs == 8) return g.rb == 1 ? launch_split<T, 1, 1>(a, stream, g) : launch_split<T, 1, 2>(a, stream, g);
+  return g.rb == 1 ? launch_split<T, 2, 1>(a, stream, g) : launch_split<T, 2, 2>(a, stream, g);
 }
 
 }  // namespace
-
-int64_t decode_split_workspace_bytes(const ic_decode_args& a) {
-  const int ntot = a.tiers.budget + 1;
-  const int Hkv = a.pool.num_kv_heads;
-  const int G = Hkv > 0 ? a.num_q_heads / Hkv : 0;
-  // the larger of the two chunk shapes, so any split_rows setting fits
-  size_t need = 0;
-  for (int rows : {64, 128}) {
-    const SplitGeom g = split_geometry(ntot, G, rows);
-    if (g.splits > SP_MAX_SPLITS) continue;
-    const size_t b = split_workspace_bytes(a.sess.num_sessions, Hkv, g);
-    if (b > need) need = b;
-  }
-  return static_cast<int64_t>(need);
-}
 
 int launch_decode_split(const ic_decode_args& a, cudaStream_t stream) {
   const int G = a.num_q_heads / a.pool.num_kv_heads;
@@ -579,36 +561,25 @@ int launch_decode_split(const ic_decode_args& a, cudaStream_t stream) {
     set_last_error("decode (split): at most 16 query heads per KV head");
     return IC_ERR_UNSUPPORTED;
   }
-  if (a.split_rows != 0 && a.split_rows != 64 && a.split_rows != 128) {
-    set_last_error("decode (split): split_rows must be 0, 64 or 128");
+  if (a.cluster_size < 0 || a.cluster_size > SP_MAXCL) {
+    set_last_error("decode (split): cluster_size must be 0 (choose) or 1..16");
     return IC_ERR_INVALID_ARG;
   }
-  const int ntot = a.tiers.budget + 1;
-  const SplitGeom g = split_geometry(ntot, G, a.split_rows);
-  if (g.splits > SP_MAX_SPLITS) {
-    set_last_error("decode (split): budget too large (at most 64 chunks of 128 slots)");
+  const int hs = G <= 8 ? 8 : 16;
+  const SplitGeom g = split_geometry(a.tiers.budget + 1, hs, a.cluster_size);
+  if (g.blocks > 2 * SP_MAXW || g.cl > SP_MAXCL) {
+    set_last_error("decode (split): budget too large for 16 CTAs of 256 slots");
     return IC_ERR_UNSUPPORTED;
   }
-  if (!a.workspace || (reinterpret_cast<uintptr_t>(a.workspace) & 255) != 0) {
-    set_last_error("decode (split): workspace must be a 256-byte aligned device buffer");
-    return IC_ERR_INVALID_ARG;
+  const SplitSmem L = split_smem(g, hs);
+  if (L.total > 227 * 1024) {
+    set_last_error("decode (split): chunk too large for one CTA's shared memory");
+    return IC_ERR_UNSUPPORTED;
   }
-  if (a.workspace_bytes < static_cast<int64_t>(split_workspace_bytes(a.sess.num_sessions, a.pool.num_kv_heads, g))) {
-    set_last_error("decode (split): workspace smaller than ic_decode_workspace_bytes()");
-    return IC_ERR_INVALID_ARG;
-  }
-  if (a.pool.dtype == IC_F16) return split_dispatch<__half>(a, stream, g);
-  if (a.pool.dtype == IC_BF16) return split_dispatch<__nv_bfloat16>(a, stream, g);
+  if (a.pool.dtype == IC_F16) return split_dispatch<__half>(a, stream, g, hs);
+  if (a.pool.dtype == IC_BF16) return split_dispatch<__nv_bfloat16>(a, stream, g, hs);
   set_last_error("decode (split): dtype must be fp16 or bf16");
   return IC_ERR_INVALID_ARG;
 }
 
 }  // namespace ic
-
-extern "C" int64_t ic_decode_workspace_bytes(const ic_decode_args* a) {
-  if (!a || a->pool.num_kv_heads <= 0 || a->num_q_heads <= 0 || a->tiers.budget <= 0 || a->sess.num_sessions < 0) {
-    ic::set_last_error("decode_workspace_bytes: bad sizes");
-    return IC_ERR_INVALID_ARG;
-  }
-  return ic::decode_split_workspace_bytes(*a);
-}

@@ -149,8 +149,6 @@ class SessionBatch:
         self.scale = cfg.head_dim ** -0.5
         self.cluster_size = 0
         self.kernel_variant = _lib.IC_DECODE_AUTO
-        self.split_rows = 0  # slot-split kernel (one layer at a time): 0 = choose, 64 or 128
-        self._workspace = None
 
         self._c_tiers = _lib.ic_tiers(cfg.sink_size, cfg.recent_size, cfg.important_size, B)
         self._c_sess = _lib.ic_sessions(num_sessions=S, slot_table=self.slot_table.data_ptr(),
@@ -168,9 +166,6 @@ class SessionBatch:
         # programmatic dependent launch between the step's kernels
         self.pdl = True
         self._step = _lib.ic_step_args(layer0=self._dec, evict=self._ev)
-        # partials of the slot-split decode kernel that attend() launches, sized
-        # for up to 8 query heads per KV head (grown on first use beyond that)
-        self._ensure_workspace(8 * cfg.num_kv_heads)
 
     # ---- hot path -------------------------------------------------------------------
     def attend(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -205,29 +200,12 @@ class SessionBatch:
         _lib.call("ic_decode_layer", d)
         return out
 
-    def _ensure_workspace(self, num_q_heads: int) -> None:
-        """The slot-split decode kernel's workspace (``ic_decode_workspace_bytes``):
-        zero-filled once; the kernel leaves its counters at zero after every
-        launch, so the buffer is reused by every layer and step."""
-        a = _lib.ic_decode_args(pool=self._c_pool, tiers=self._c_tiers)
-        a.sess.num_sessions = self.num_sessions
-        a.num_q_heads = num_q_heads
-        need = _lib.size_query("ic_decode_workspace_bytes", a)
-        if self._workspace is None or self._workspace.numel() < need:
-            # 256-byte aligned: torch's CUDA allocator returns 512-byte aligned blocks
-            self._workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
-
     def _prepare_decode(self, d: "_lib.ic_decode_args", Hq: int) -> None:
         """Set the launch options of one decode call on `d`."""
         d.num_q_heads = Hq
         d.cluster_size = self.cluster_size
         d.kernel_variant = self.kernel_variant
         d.pdl = 1 if self.pdl else 0
-        if Hq > 8 * self.cfg.num_kv_heads:
-            self._ensure_workspace(Hq)
-        d.split_rows = self.split_rows
-        d.workspace = self._workspace.data_ptr()
-        d.workspace_bytes = self._workspace.numel()
 
     def evict(self, positions, decay: Optional[float] = None, use_mass: bool = True) -> None:
         """Kernel B once per step after the last layer.  positions: [S] int64

@@ -22,7 +22,7 @@ def declared_functions():
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.ic_abi_version() == 3
+    assert lib.ic_abi_version() == 2
 
 
 def test_exports_every_declared_symbol():
@@ -32,8 +32,7 @@ def test_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     # and the binding covers exactly the declared entry points
-    assert set(names) == (set(_lib.ENTRY_POINTS) | set(_lib.INFO_ENTRY_POINTS) | set(_lib.HOST_ENTRY_POINTS)
-                          | set(_lib.SIZE_ENTRY_POINTS))
+    assert set(names) == set(_lib.ENTRY_POINTS) | set(_lib.INFO_ENTRY_POINTS) | set(_lib.HOST_ENTRY_POINTS)
 
 
 def test_status_strings():
@@ -56,24 +55,6 @@ def test_null_args_rejected_without_launch():
     lib = _lib.load()
     for name in _lib.ENTRY_POINTS:
         assert getattr(lib, name)(None, None) == _lib.IC_ERR_INVALID_ARG, name
-
-
-def test_decode_workspace_size_is_host_only():
-    """The slot-split decode variant's workspace size needs no device: per
-    (session, KV head) one counter and, per 64-slot chunk, 8 heads x (max, sum,
-    128 outputs, 64 scores) floats."""
-    lib = _lib.load()
-    assert lib.ic_decode_workspace_bytes(None) == _lib.IC_ERR_INVALID_ARG
-    a = _lib.ic_decode_args()
-    a.pool.num_kv_heads, a.num_q_heads = 2, 16
-    a.tiers = _lib.ic_tiers(4, 256, 780, 1040)
-    a.sess.num_sessions = 16
-    n = _lib.size_query("ic_decode_workspace_bytes", a)
-    groups, splits = 32, -(-1041 // 64)
-    assert n == 256 + groups * splits * 8 * (2 + 128 + 64) * 4
-    a.tiers = _lib.ic_tiers(0, 0, 0, 0)
-    with pytest.raises(_lib.InvalidArgument):
-        _lib.size_query("ic_decode_workspace_bytes", a)
 
 
 def test_struct_layout_matches_c():

@@ -580,8 +580,8 @@ def _c2_prompts(L, Hkv, D, S, T, seed):
              torch.rand(T, generator=g)) for _ in range(S)], g
 
 
-@pytest.mark.parametrize("split_rows", [0, 64, 128])
-def test_attend_layer_at_a_time_vs_oracle(split_rows):
+@pytest.mark.parametrize("cluster", [0, 8, 9, 14])
+def test_attend_layer_at_a_time_vs_oracle(cluster):
     """One layer at a time, as a decoder forward calls it (attend per layer,
     q of a layer only after the previous layer: no inputs_ready), which runs
     the slot-split kernel: the bench workload's shapes (36 layers, 16 sessions,
@@ -602,7 +602,7 @@ def test_attend_layer_at_a_time_vs_oracle(split_rows):
     def build(variant):
         b = SessionBatch(cfg, S, "cuda:0")
         b.kernel_variant = variant
-        b.split_rows = split_rows
+        b.cluster_size = cluster if variant == _lib.IC_DECODE_AUTO else 0
         for s in range(S):
             b.load_prompt(s, tuple((prompts[s][0][l][None].cuda(), prompts[s][1][l][None].cuda())
                                    for l in range(L)), prompts[s][2])
@@ -664,7 +664,8 @@ def run_small_attend(sp, dtype):
     qd, kd, vd = q.to(dt).cuda(), k.to(dt).cuda(), v.to(dt).cuda()
     outs, events = [], []
     for s in range(sp["steps"]):
-        o = torch.stack([cache.attend(l, qd[s, l], kd[s, l], vd[s, l]) for l in range(sp["layers"])])
+        o = torch.stack([cache.attend(l, qd[s, l], kd[s, l], vd[s, l], out_dtype=torch.float32)
+                         for l in range(sp["layers"])])
         cache.evict(T + s)
         oo, ev = decode_step(oc, q[s].numpy(), k[s].numpy(), v[s].numpy(), T + s, sp["decay"])
         g = o.float().cpu().numpy()
