@@ -16,11 +16,13 @@ under a lock, paged_cache.py:205-288).
 """
 from __future__ import annotations
 
+import heapq
 import threading
 import time
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Tuple
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -140,83 +142,166 @@ class PagePool:
         return K[0], V[0]
 
 
+@dataclass
+class _Lease:
+    """One session's hold on the pool: its pages in allocation order, the clock
+    value of its last use and its creation rank (which orders equal clock
+    values the way a dict of sessions in creation order would)."""
+    pages: List[int] = field(default_factory=list)
+    stamp: float = 0.0
+    rank: int = 0
+
+
 class KVAllocator:
-    """Thread-safe LIFO free-list page allocator with LRU session eviction
-    (paged_cache.py:205-288).  ``clock`` replaces time.monotonic when given."""
+    """Page allocator with least-recently-used session eviction
+    (paged_cache.py:205-288).
+
+    Free pages form a stack (an int32 array and a top index): the initial
+    stack holds page ids 0 .. n-1 with n-1 on top, a released session's pages
+    are pushed back in their allocation order, and an allocation takes the top
+    page -- the reference's free-list order.  Each session with pages holds a
+    ``_Lease``.  Eviction victims come from a heap of (last use, creation rank,
+    session) entries; a touch pushes a new entry and the stale ones are
+    skipped when they surface, so finding the least recently used session is
+    O(log n) instead of a scan over all sessions.  Equal last-use values go to
+    the earliest-created lease, as a minimum over a creation-ordered dict
+    would.  ``clock`` replaces time.monotonic (tests pass a counter).  All
+    methods hold one lock."""
 
     def __init__(self, n_pages: int, max_pages_per_session: int, clock=None) -> None:
-        self._max_pps = max_pages_per_session
-        self._lock = threading.Lock()
-        self._free_list: List[int] = list(range(n_pages))
-        self._session_pages: Dict[str, List[int]] = {}
-        self._session_atime: Dict[str, float] = {}
-        self._session_ntok: Dict[str, int] = {}
-        self._clock = clock or time.monotonic
+        self.n_pages = int(n_pages)
+        self.max_pages_per_session = int(max_pages_per_session)
+        self._stack = np.arange(self.n_pages, dtype=np.int32)
+        self._top = self.n_pages
+        self._leases: Dict[str, _Lease] = {}
+        self._tokens: Dict[str, int] = {}
+        self._lru: List[Tuple[float, int, str]] = []
+        self._next_rank = 0
+        self._now = clock or time.monotonic
+        self._mu = threading.Lock()
         self.lru_evictions = 0
 
-    def _evict_lru(self) -> None:
-        if not self._session_pages:
-            raise RuntimeError("PagePool exhausted and no sessions to evict")
-        lru_session = min(self._session_atime, key=self._session_atime.__getitem__)
-        self._release_locked(lru_session)
-        self.lru_evictions += 1
+    # -- internals (lock held) --------------------------------------------------------
+    def _stamp(self, session_id: str, lease: _Lease) -> None:
+        lease.stamp = self._now()
+        heapq.heappush(self._lru, (lease.stamp, lease.rank, session_id))
 
-    def _release_locked(self, session_id: str) -> None:
-        pages = self._session_pages.pop(session_id, [])
-        self._free_list.extend(pages)
-        self._session_atime.pop(session_id, None)
-        self._session_ntok.pop(session_id, None)
+    def _drop(self, session_id: str) -> None:
+        lease = self._leases.pop(session_id, None)
+        self._tokens.pop(session_id, None)
+        if lease is not None and lease.pages:
+            n = len(lease.pages)
+            self._stack[self._top:self._top + n] = lease.pages
+            self._top += n
 
+    def _victim(self) -> str:
+        while self._lru:
+            stamp, rank, sid = heapq.heappop(self._lru)
+            lease = self._leases.get(sid)
+            if lease is not None and lease.rank == rank and lease.stamp == stamp:
+                return sid
+        raise RuntimeError("PagePool exhausted and no sessions to evict")
+
+    def _take(self, session_id: str) -> int:
+        lease = self._leases.get(session_id)
+        if lease is not None and len(lease.pages) >= self.max_pages_per_session:
+            raise RuntimeError(f"Session {session_id!r} exceeded max pages ({self.max_pages_per_session})")
+        if self._top == 0:
+            if not self._leases:
+                raise RuntimeError("PagePool exhausted and no sessions to evict")
+            self._drop(self._victim())
+            self.lru_evictions += 1
+            lease = self._leases.get(session_id)
+        if lease is None:
+            lease = self._leases[session_id] = _Lease(rank=self._next_rank)
+            self._next_rank += 1
+        self._top -= 1
+        page = int(self._stack[self._top])
+        lease.pages.append(page)
+        self._stamp(session_id, lease)
+        if len(self._lru) > 4 * len(self._leases) + 64:  # drop stale heap entries now and then
+            self._lru = [(lz.stamp, lz.rank, sid) for sid, lz in self._leases.items()]
+            heapq.heapify(self._lru)
+        return page
+
+    # -- the reference's interface -------------------------------------------------------
     def allocate_page(self, session_id: str) -> int:
-        with self._lock:
-            cur_pages = len(self._session_pages.get(session_id, []))
-            if cur_pages >= self._max_pps:
-                raise RuntimeError(f"Session {session_id!r} exceeded max pages ({self._max_pps})")
-            if not self._free_list:
-                self._evict_lru()
-            page_id = self._free_list.pop()
-            self._session_pages.setdefault(session_id, []).append(page_id)
-            self._session_atime[session_id] = self._clock()
-            return page_id
+        """One page for `session_id`; evicts the least recently used session when
+        no page is free.  RuntimeError at the per-session cap or when nothing can
+        be evicted."""
+        with self._mu:
+            return self._take(session_id)
+
+    def allocate_pages(self, session_id: str, count: int) -> Tuple[List[int], Optional[RuntimeError]]:
+        """``count`` consecutive allocate_page calls under one lock acquisition:
+        the pages obtained before any failure, and that failure (or None)."""
+        got: List[int] = []
+        with self._mu:
+            for _ in range(count):
+                try:
+                    got.append(self._take(session_id))
+                except RuntimeError as e:
+                    return got, e
+        return got, None
 
     def touch(self, session_id: str) -> None:
-        with self._lock:
-            if session_id in self._session_atime:
-                self._session_atime[session_id] = self._clock()
+        with self._mu:
+            lease = self._leases.get(session_id)
+            if lease is not None:
+                self._stamp(session_id, lease)
 
     def release_session(self, session_id: str) -> None:
-        with self._lock:
-            self._release_locked(session_id)
+        with self._mu:
+            self._drop(session_id)
 
     def set_token_count(self, session_id: str, n: int) -> None:
-        with self._lock:
-            self._session_ntok[session_id] = n
+        with self._mu:
+            self._tokens[session_id] = int(n)
 
     def get_token_count(self, session_id: str) -> int:
-        with self._lock:
-            return self._session_ntok.get(session_id, 0)
+        with self._mu:
+            return self._tokens.get(session_id, 0)
 
     def pages_for(self, session_id: str) -> List[int]:
-        with self._lock:
-            return list(self._session_pages.get(session_id, []))
+        with self._mu:
+            lease = self._leases.get(session_id)
+            return list(lease.pages) if lease is not None else []
 
     def utilization(self) -> float:
-        with self._lock:
-            total_pages = sum(len(v) for v in self._session_pages.values())
-            n_pages = total_pages + len(self._free_list)
-            return total_pages / n_pages if n_pages else 0.0
+        with self._mu:
+            return (self.n_pages - self._top) / self.n_pages if self.n_pages else 0.0
 
     def active_sessions(self) -> List[str]:
-        with self._lock:
-            return list(self._session_pages.keys())
+        with self._mu:
+            return list(self._leases)
 
+    # -- additions ---------------------------------------------------------------------
     def free_pages(self) -> int:
-        with self._lock:
-            return len(self._free_list)
+        with self._mu:
+            return self._top
+
+    def free_list(self) -> List[int]:
+        """The free pages bottom to top (the next allocation takes the last)."""
+        with self._mu:
+            return self._stack[:self._top].tolist()
+
+    def fragmentation(self, page_size: int = PAGE_SIZE) -> float:
+        """Allocated-but-empty token slots / allocated token slots, from the token
+        counts the sessions report (set_token_count)."""
+        with self._mu:
+            held = sum(len(lz.pages) for lz in self._leases.values()) * page_size
+            if held == 0:
+                return 0.0
+            used = sum(min(self._tokens.get(sid, 0), len(lz.pages) * page_size) for sid, lz in self._leases.items())
+            return (held - used) / held
 
 
 class PagedSessionView:
-    """Append-only view of one session's pages (paged_cache.py:293-396)."""
+    """Append-only view of one session's pages (paged_cache.py:293-396).
+
+    Token metadata lives in growable numpy arrays; a push allocates its pages
+    in one allocator call and writes every layer and token in one kernel
+    launch (``PagePool.write_rows``)."""
 
     def __init__(self, session_id: str, pool: PagePool, allocator: KVAllocator) -> None:
         self.session_id = session_id
@@ -224,42 +309,52 @@ class PagedSessionView:
         self._alloc = allocator
         self._pages: List[int] = []
         self._n_tokens: int = 0
-        self._importance: List[float] = []
-        self._positions: List[int] = []
+        self._pos = np.zeros(0, dtype=np.int64)
+        self._imp = np.zeros(0, dtype=np.float64)
         self._lock = threading.Lock()
 
     @property
     def n_tokens(self) -> int:
         return self._n_tokens
 
+    def _grow(self, n: int) -> None:
+        if n > self._pos.shape[0]:
+            cap = max(n, 2 * self._pos.shape[0], 64)
+            pos = np.zeros(cap, dtype=np.int64)
+            imp = np.zeros(cap, dtype=np.float64)
+            pos[:self._n_tokens] = self._pos[:self._n_tokens]
+            imp[:self._n_tokens] = self._imp[:self._n_tokens]
+            self._pos, self._imp = pos, imp
+
     def push(self, k_states: torch.Tensor, v_states: torch.Tensor, positions: List[int],
              importance: List[float]) -> None:
         """Write T tokens [n_layers, n_heads, T, head_dim] (paged_cache.py:330-363).
 
-        Pages are allocated in the reference's order (one whenever a token
-        starts a page).  If an allocation raises, the tokens that fit in the
-        pages obtained so far are still written and counted, as in the
-        reference's token-by-token loop, and the error propagates.
+        A page is allocated whenever a token starts one, in the reference's
+        order.  If an allocation fails, the tokens that fit in the pages
+        obtained so far are still written and counted, as the reference's
+        token-by-token loop does, and the error propagates.  Missing positions
+        continue the token count; missing importance values are 0.
         """
-        n_new = k_states.shape[2]
+        n_new = int(k_states.shape[2])
         with self._lock:
             start = self._n_tokens
-            fit = 0
-            err: Optional[BaseException] = None
-            for t in range(n_new):
-                if (start + t) % PAGE_SIZE == 0:
-                    try:
-                        self._pages.append(self._alloc.allocate_page(self.session_id))
-                    except RuntimeError as e:
-                        err = e
-                        break
-                fit += 1
-            if fit:
+            room = len(self._pages) * PAGE_SIZE - start
+            need = max(0, -(-(n_new - room) // PAGE_SIZE)) if n_new > room else 0
+            got, err = self._alloc.allocate_pages(self.session_id, need) if need else ([], None)
+            self._pages.extend(got)
+            fit = min(n_new, len(self._pages) * PAGE_SIZE - start)
+            if fit > 0:
                 self._pool.write_rows(self._pages, start, k_states[:, :, :fit], v_states[:, :, :fit])
-            for t in range(fit):
-                self._n_tokens += 1
-                self._positions.append(positions[t] if t < len(positions) else self._n_tokens - 1)
-                self._importance.append(importance[t] if t < len(importance) else 0.0)
+                self._grow(start + fit)
+                idx = np.arange(fit)
+                given = np.asarray(positions[:fit], dtype=np.int64)
+                self._pos[start:start + fit] = np.where(idx < given.shape[0],
+                                                        np.pad(given, (0, fit - given.shape[0])),
+                                                        start + idx)
+                vals = np.asarray(importance[:fit], dtype=np.float64)
+                self._imp[start:start + fit] = np.pad(vals, (0, fit - vals.shape[0]))
+                self._n_tokens = start + fit
             if err is not None:
                 raise err
             self._alloc.set_token_count(self.session_id, self._n_tokens)
@@ -280,60 +375,70 @@ class PagedSessionView:
         return [(K[l][None], V[l][None]) for l in range(K.shape[0])]
 
     def top_importance_tokens(self, top_k: int) -> Tuple[List[int], List[float]]:
-        if not self._importance:
+        """Token indices and importance of the top_k tokens: highest importance
+        first, equal importance by higher index first (the order of a
+        descending sort of (importance, index) pairs)."""
+        n = self._n_tokens
+        if n == 0:
             return [], []
-        pairs = sorted(zip(self._importance, range(len(self._importance))), reverse=True)
-        top_pairs = pairs[:top_k]
-        return [p for _, p in top_pairs], [imp for imp, _ in top_pairs]
+        imp = self._imp[:n]
+        order = np.lexsort((np.arange(n), imp))[::-1][:max(0, top_k)]
+        return order.tolist(), imp[order].tolist()
 
     def reset(self) -> None:
+        """Give the pages back and forget every token."""
         with self._lock:
             self._alloc.release_session(self.session_id)
-            self._pages = []
-            self._n_tokens = 0
-            self._importance = []
-            self._positions = []
+            self._pages, self._n_tokens = [], 0
+            self._pos = np.zeros(0, dtype=np.int64)
+            self._imp = np.zeros(0, dtype=np.float64)
 
 
 class MultiSessionCache:
-    """All PagedSessionViews sharing one PagePool (paged_cache.py:401-454)."""
+    """Session views over one PagePool with one shared allocator
+    (paged_cache.py:401-454)."""
 
     def __init__(self, pool: PagePool, clock=None) -> None:
         self._pool = pool
-        self._alloc = KVAllocator(pool.cfg.n_pages, pool.cfg.max_pages_per_session, clock=clock)
-        self._views: Dict[str, PagedSessionView] = {}
-        self._lock = threading.Lock()
+        self.allocator = KVAllocator(pool.cfg.n_pages, pool.cfg.max_pages_per_session, clock=clock)
+        self._sessions: Dict[str, PagedSessionView] = {}
+        self._mu = threading.Lock()
+
+    @property
+    def _alloc(self) -> KVAllocator:
+        return self.allocator
 
     def get_or_create(self, session_id: str) -> PagedSessionView:
-        with self._lock:
-            if session_id not in self._views:
-                self._views[session_id] = PagedSessionView(session_id, self._pool, self._alloc)
-            return self._views[session_id]
+        with self._mu:
+            view = self._sessions.get(session_id)
+            if view is None:
+                view = self._sessions[session_id] = PagedSessionView(session_id, self._pool, self.allocator)
+            return view
 
     def reset(self, session_id: str) -> None:
-        with self._lock:
-            view = self._views.pop(session_id, None)
-        if view:
+        with self._mu:
+            view = self._sessions.pop(session_id, None)
+        if view is not None:
             view.reset()
 
     def reset_all(self) -> None:
-        with self._lock:
-            sessions = list(self._views.keys())
-        for sid in sessions:
+        for sid in self.sessions():
             self.reset(sid)
 
+    def sessions(self) -> List[str]:
+        """Ids of every view created and not reset (with or without pages)."""
+        with self._mu:
+            return list(self._sessions)
+
     def utilization(self) -> float:
-        return self._alloc.utilization()
+        return self.allocator.utilization()
 
     def active_sessions(self) -> List[str]:
-        return self._alloc.active_sessions()
+        return self.allocator.active_sessions()
 
     def pool_info(self) -> dict:
-        cfg = self._pool.cfg
-        return {
-            "total_pages": cfg.n_pages,
-            "total_tokens": cfg.total_tokens,
-            "gpu_memory_mb": cfg.gpu_memory_mb(),
-            "utilization": f"{self.utilization() * 100:.1f}%",
-            "active_sessions": len(self.active_sessions()),
-        }
+        """Pool size and use, with the reference's keys."""
+        c = self._pool.cfg
+        return dict(total_pages=c.n_pages, total_tokens=c.total_tokens, gpu_memory_mb=c.gpu_memory_mb(),
+                    utilization="%.1f%%" % (100.0 * self.utilization()),
+                    active_sessions=len(self.active_sessions()))

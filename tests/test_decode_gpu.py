@@ -545,11 +545,11 @@ def test_paged_trace_gpu(golden):
             elif op[0] == "reset":
                 msc.reset(op[1])
             elif op[0] == "touch":
-                msc._alloc.touch(op[1])
+                msc.allocator.touch(op[1])
         except RuntimeError as e:
             err = str(e)
         assert err == str(g["errors"][i]), (i, op)
-        pages = {s: msc._alloc.pages_for(s) for s in sorted(msc.active_sessions())}
+        pages = {s: msc.allocator.pages_for(s) for s in sorted(msc.active_sessions())}
         assert pages == json.loads(str(g["pages"][i])), (i, op)
         assert abs(msc.utilization() - float(g["util"][i])) < 1e-12
     assert np.array_equal(np.concatenate(gathers), g["gathers"])

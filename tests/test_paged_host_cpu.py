@@ -50,13 +50,13 @@ def test_allocation_trace_matches_reference(golden):
             elif op[0] == "reset":
                 msc.reset(op[1])
             elif op[0] == "touch":
-                msc._alloc.touch(op[1])
+                msc.allocator.touch(op[1])
         except RuntimeError as e:
             err = str(e)
         assert err == str(g["errors"][i]), (i, op, err)
-        pages = {s: msc._alloc.pages_for(s) for s in sorted(msc.active_sessions())}
+        pages = {s: msc.allocator.pages_for(s) for s in sorted(msc.active_sessions())}
         assert pages == json.loads(str(g["pages"][i])), (i, op)
-        assert msc._alloc._free_list == json.loads(str(g["free"][i])), (i, op)
+        assert msc.allocator.free_list() == json.loads(str(g["free"][i])), (i, op)
         assert abs(msc.utilization() - float(g["util"][i])) < 1e-12
 
 
@@ -73,7 +73,7 @@ def test_partial_push_on_cap_keeps_what_fits():
         view.push(kk, kk, positions=list(range(n)), importance=[0.0] * n)
     assert view.n_tokens == sp["max_pps"] * 16
     assert msc._pool.writes[-1][2] == sp["max_pps"] * 16
-    assert len(msc._alloc.pages_for("S")) == sp["max_pps"]
+    assert len(msc.allocator.pages_for("S")) == sp["max_pps"]
 
 
 def test_allocator_lifo_lru_and_exhaustion():
@@ -96,3 +96,80 @@ def test_allocator_lifo_lru_and_exhaustion():
     b = KVAllocator(0, 4)
     with pytest.raises(RuntimeError, match="PagePool exhausted and no sessions to evict"):
         b.allocate_page("s")
+
+
+def test_allocator_matches_oracle_on_random_ops():
+    """Random allocations, touches and releases over a small pool: the same
+    pages, free-stack order, active sessions, utilization and errors as the
+    oracle's restatement of the reference allocator (paged_cache.py:205-288)."""
+    import random
+    from oracle.paged import OracleAllocator
+    rng = random.Random(5)
+    for trial in range(20):
+        n_pages, cap = rng.randint(1, 24), rng.randint(1, 8)
+        oa = OracleAllocator(n_pages, cap)
+        ticks = iter(range(1, 10 ** 6))
+        ka = KVAllocator(n_pages, cap, clock=lambda: float(next(ticks)))
+        sids = [f"s{i}" for i in range(rng.randint(1, 6))]
+        for step in range(300):
+            op, sid = rng.random(), rng.choice(sids)
+            if op < 0.7:
+                res = []
+                for a in (oa, ka):
+                    try:
+                        res.append(a.allocate_page(sid))
+                    except RuntimeError as e:
+                        res.append(str(e))
+                assert res[0] == res[1], (trial, step, res)
+            elif op < 0.85:
+                oa.touch(sid)
+                ka.touch(sid)
+            else:
+                oa._release(sid)
+                ka.release_session(sid)
+            assert ka.free_list() == oa.free, (trial, step)
+            assert ka.active_sessions() == list(oa.pages), (trial, step)
+            for s in sids:
+                assert ka.pages_for(s) == oa.pages.get(s, [])
+            assert abs(ka.utilization() - oa.utilization()) < 1e-12
+
+
+def test_lru_equal_clock_values_evict_earliest_created():
+    """With a clock that does not advance, the victim is the session created
+    first among those holding pages (a minimum over a creation-ordered map)."""
+    a = KVAllocator(3, 4, clock=lambda: 7.0)
+    a.allocate_page("x")
+    a.allocate_page("y")
+    a.allocate_page("z")
+    a.touch("x")
+    assert a.allocate_page("w") == 2      # x (created first) is evicted; its page 2 is reused
+    assert a.active_sessions() == ["y", "z", "w"] and a.lru_evictions == 1
+    a.release_session("y")                # page 1 back on the stack
+    assert a.allocate_page("x") == 1      # x comes back as a new, latest-created lease
+    assert a.allocate_page("v") == 0      # no free page: z, the earliest-created holder, goes
+    assert a.allocate_page("u") == 2      # then w
+    assert a.active_sessions() == ["x", "v", "u"] and a.lru_evictions == 3
+
+
+def test_fragmentation_and_batched_allocation():
+    a = KVAllocator(10, 4)
+    got, err = a.allocate_pages("s", 3)
+    assert got == [9, 8, 7] and err is None
+    a.set_token_count("s", 33)                       # 48 slots held, 33 used
+    assert abs(a.fragmentation() - 15 / 48) < 1e-12
+    got, err = a.allocate_pages("s", 3)              # cap 4: one more, then the cap error
+    assert got == [6] and "exceeded max pages" in str(err)
+
+
+def test_top_importance_tokens_order_matches_oracle():
+    from oracle.paged import OracleAllocator, OracleMultiSession, OraclePagePool
+    sp = specs.PAGED
+    msc = _msc()
+    view = msc.get_or_create("S")
+    imp = [0.5, 0.25, 0.5, 1.0, 0.0, 0.25, 1.0, 0.5]
+    kk = torch.zeros(sp["layers"], sp["heads"], len(imp), sp["d"])
+    view.push(kk, kk, positions=list(range(len(imp))), importance=imp)
+    pairs = sorted(zip(imp, range(len(imp))), reverse=True)
+    for k in (0, 3, 8, 20):
+        idx, vals = view.top_importance_tokens(k)
+        assert idx == [i for _, i in pairs[:k]] and vals == [x for x, _ in pairs[:k]]
