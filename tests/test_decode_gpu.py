@@ -64,8 +64,8 @@ def test_wide_budget_vs_oracle(variant):
 def test_small_protocol_variants(name, variant):
     """Every kernel-A implementation (CUDA cores; tensor cores with one
     cluster per group; tensor cores streaming a group per CTA; four warp
-    pipelines per group; CTAs over slot chunks merged by the last to finish)
-    against the oracle."""
+    pipelines per group; a cluster of CTAs over slot chunks merged through
+    distributed shared memory) against the oracle."""
     cache, oc, outs, events = run_small(name, variant=variant)
     cache.batch.check_device_status()
 
@@ -580,15 +580,17 @@ def _c2_prompts(L, Hkv, D, S, T, seed):
              torch.rand(T, generator=g)) for _ in range(S)], g
 
 
-@pytest.mark.parametrize("cluster", [0, 8, 9, 14])
-def test_attend_layer_at_a_time_vs_oracle(cluster):
+@pytest.mark.parametrize("variant,knob", [(0, 0), (5, 8), (5, 14)])
+def test_attend_layer_at_a_time_vs_oracle(variant, knob):
     """One layer at a time, as a decoder forward calls it (attend per layer,
     q of a layer only after the previous layer: no inputs_ready), which runs
-    the slot-split kernel: the bench workload's shapes (36 layers, 16 sessions,
-    16/2 heads, budget 4/256/780, fp16, 2048-token prompts).  Session 0 against
-    the oracle step by step; every session against the cluster kernel (events
-    equal, outputs and importance within 1e-3); a second run reproduces every
-    output bit for bit (the last CTA merges the chunks in chunk order)."""
+    the slot-split kernel (a cluster of CTAs merging through distributed shared
+    memory, cluster_size = knob): the bench
+    workload's shapes (36 layers, 16 sessions, 16/2 heads, budget 4/256/780,
+    fp16, 2048-token prompts).  Session 0 against the oracle step by step;
+    every session against the one-cluster-per-group kernel (events equal,
+    outputs and importance within 1e-3); a second run reproduces every output
+    bit for bit (the chunks are merged in chunk order)."""
     from infercache_b200 import CacheConfig, SessionBatch
     from infercache_b200 import _lib
     L, Hq, Hkv, D, S, T, steps = 36, 16, 2, 128, 16, 2048, 4
@@ -602,7 +604,8 @@ def test_attend_layer_at_a_time_vs_oracle(cluster):
     def build(variant):
         b = SessionBatch(cfg, S, "cuda:0")
         b.kernel_variant = variant
-        b.cluster_size = cluster if variant == _lib.IC_DECODE_AUTO else 0
+        if variant == _lib.IC_DECODE_TENSOR_SPLIT:
+            b.cluster_size = knob
         for s in range(S):
             b.load_prompt(s, tuple((prompts[s][0][l][None].cuda(), prompts[s][1][l][None].cuda())
                                    for l in range(L)), prompts[s][2])
@@ -624,7 +627,7 @@ def test_attend_layer_at_a_time_vs_oracle(cluster):
                 assert tuple(b.events[0].tolist()) == e.as_tuple(), t
         return outs, evs
 
-    b1 = build(_lib.IC_DECODE_AUTO)
+    b1 = build(variant)
     oc = OracleCache(TierGeometry(L, Hkv, D, 4, 256, 780), np.float16)
     oc.load_from_hf_output(prompts[0][0].float().numpy(), prompts[0][1].float().numpy(), prompts[0][2].numpy())
     outs1, evs1 = run(b1, oc)
@@ -640,7 +643,7 @@ def test_attend_layer_at_a_time_vs_oracle(cluster):
     assert torch.equal(b1.slot_table, b2.slot_table)
     assert elem_close(b1.importance.cpu().numpy(), b2.importance.cpu().numpy(), 1e-3)
     # bit-for-bit reproducible
-    b3 = build(_lib.IC_DECODE_AUTO)
+    b3 = build(variant)
     outs3, _ = run(b3)
     for t in range(steps):
         assert torch.equal(outs1[t], outs3[t]), t
@@ -648,7 +651,7 @@ def test_attend_layer_at_a_time_vs_oracle(cluster):
     b3.check_device_status()
 
 
-def run_small_attend(sp, dtype):
+def run_small_attend(sp, dtype, variant=0):
     """run_small with each step taken layer by layer through attend()."""
     from gpu_protocol import TORCH_DT
     dt = TORCH_DT[dtype]
@@ -656,6 +659,7 @@ def run_small_attend(sp, dtype):
     pk, pv, q, k, v = (t.to(dt).float() for t in (pk, pv, q, k, v))
     cache = make_gpu_cache(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"], dt,
                            sp["decay"])
+    cache.batch.kernel_variant = variant
     oc = OracleCache(TierGeometry(sp["layers"], sp["hkv"], sp["d"], sp["sink"], sp["recent"], sp["important"]),
                      np.float32)
     cache.load_from_hf_output(tuple((pk[l][None].to(dt), pv[l][None].to(dt)) for l in range(sp["layers"])), scores)
@@ -677,13 +681,14 @@ def run_small_attend(sp, dtype):
     return cache, oc, np.stack(outs), np.array(events, np.int64)
 
 
+@pytest.mark.parametrize("variant", [0, 5])
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
 @pytest.mark.parametrize("hq", [8, 32])
-def test_attend_split_kernel_small(dtype, hq):
+def test_attend_split_kernel_small(dtype, hq, variant):
     """The slot-split kernel layer at a time on a small primed cache, with 4
     and 16 query heads per KV head (one and two n = 8 blocks), fp16 and bf16,
     against the oracle on inputs rounded to the cache dtype."""
     sp = dict(specs.SMALL["f16"])
     sp.update(hq=hq, hkv=2)
-    cache, oc, outs, events = run_small_attend(sp, dtype)
+    cache, oc, outs, events = run_small_attend(sp, dtype, variant)
     cache.batch.check_device_status()
