@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define IC_ABI_VERSION 2
+#define IC_ABI_VERSION 3
 
 /* Status codes.  The Python layer maps them to the reference's exception
  * types: RuntimeError for exhaustion / cap (paged_cache.py:229, 244),
@@ -69,7 +69,9 @@ enum ic_counter {
   IC_CNT_EVICTIONS = 1,
   IC_CNT_STEPS = 2,
   IC_CNT_PROMOTIONS = 3,
-  IC_COUNTER_WORDS = 4
+  IC_CNT_NEAR_TIES = 4,    /* eviction decisions whose two smallest L2 scores
+                              were within 1e-6 relative (words 5-7 reserved) */
+  IC_COUNTER_WORDS = 8
 };
 
 /* kinds in an event record {kind, displaced_pos, target_slot, evicted_pos} */

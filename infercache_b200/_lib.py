@@ -31,9 +31,9 @@ IC_ERR_NO_DEVICE = -9
 IC_F32, IC_F16, IC_BF16 = 0, 1, 2
 IC_CTRL_SINK_FILL, IC_CTRL_RECENT_FILL, IC_CTRL_RECENT_PTR, IC_CTRL_IMPORTANT_FILL = 0, 1, 2, 3
 IC_CTRL_WORDS = 8
-IC_CNT_TOKENS_SEEN, IC_CNT_EVICTIONS, IC_CNT_STEPS, IC_CNT_PROMOTIONS = 0, 1, 2, 3
+IC_CNT_TOKENS_SEEN, IC_CNT_EVICTIONS, IC_CNT_STEPS, IC_CNT_PROMOTIONS, IC_CNT_NEAR_TIES = 0, 1, 2, 3, 4
 IC_SUMMARY_STATIC_MASS_MAX = 4194304  # floats of ic_summary_score_static's static scratch
-IC_COUNTER_WORDS = 4
+IC_COUNTER_WORDS = 8
 IC_EV_NONE, IC_EV_DROP, IC_EV_FILL, IC_EV_EVICT, IC_EV_REJECT = 0, 1, 2, 3, 4
 IC_DEVFLAG_TIMEOUT, IC_DEVFLAG_BAD_ROW = 1, 2
 IC_DECODE_AUTO, IC_DECODE_CUDA_CORES, IC_DECODE_TENSOR_CORES, IC_DECODE_TENSOR_STREAM = 0, 1, 2, 3

@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   __shared__ float red_v[EV_THREADS / 32];
   __shared__ int red_i[EV_THREADS / 32];
   __shared__ int amin_slot;
+  __shared__ float runner_up;
 
   const int s = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -174,6 +175,20 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
       if (lane == 0) amin_slot = bi;
     }
     __syncthreads();
+    // the runner-up score, to count decisions that rest on a near-tie
+    float sv = __int_as_float(0x7f800000);
+    for (int j = l2s + tid; j < l2s + l2fill; j += EV_THREADS)
+      if (j != amin_slot) sv = fminf(sv, imp_s[j]);
+    sv = warp_min(sv);
+    __syncthreads();  // red_v is reused
+    if (lane == 0) red_v[warp] = sv;
+    __syncthreads();
+    if (warp == 0) {
+      sv = lane < EV_THREADS / 32 ? red_v[lane] : __int_as_float(0x7f800000);
+      sv = warp_min(sv);
+      if (lane == 0) runner_up = sv;
+    }
+    __syncthreads();
   }
 
   // 3. apply the decision (one thread, from the staged copies)
@@ -182,6 +197,7 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
     const int32_t row_r = stt_s[r], row_s = stt_s[B];
     int32_t new_stage = row_r;
     int64_t evictions = snap_cnt[IC_CNT_EVICTIONS], promotions = snap_cnt[IC_CNT_PROMOTIONS];
+    int64_t near_ties = snap_cnt[IC_CNT_NEAR_TIES];
     if (displaced) {
       dpos = pos_s[r];
       int tgt = -1;
@@ -193,6 +209,8 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
         kind = IC_EV_FILL;
       } else if (cap > 0) {
         target = amin_slot;
+        const float lo = imp_s[amin_slot];
+        if (l2fill > 1 && runner_up - lo <= 1e-6f * fabsf(lo)) near_ties += 1;
         if (score > imp_s[amin_slot]) {
           tgt = amin_slot;
           kind = IC_EV_EVICT;
@@ -226,6 +244,7 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
     cnt[IC_CNT_STEPS] = snap_cnt[IC_CNT_STEPS] + 1;
     cnt[IC_CNT_EVICTIONS] = evictions;
     cnt[IC_CNT_PROMOTIONS] = promotions;
+    cnt[IC_CNT_NEAR_TIES] = near_ties;
     if (a.events) {
       int64_t* e = a.events + static_cast<size_t>(s) * 4;
       e[0] = kind; e[1] = dpos; e[2] = target; e[3] = epos;

@@ -88,6 +88,9 @@ class CacheStats:
     recent_fill: int = 0
     important_fill: int = 0
     total_promotions: int = 0  # tokens moved from the recent ring into the importance tier
+    # eviction decisions whose two smallest importance-tier scores were within
+    # 1e-6 relative: decisions that float summation order could flip
+    near_ties: int = 0
 
 
 def _check_cfg(cfg: CacheConfig) -> None:
@@ -449,7 +452,7 @@ class SessionBatch:
         sf, rf, imf = c[_lib.IC_CTRL_SINK_FILL], c[_lib.IC_CTRL_RECENT_FILL], c[_lib.IC_CTRL_IMPORTANT_FILL]
         return CacheStats(total_tokens_seen=n[_lib.IC_CNT_TOKENS_SEEN], total_evictions=n[_lib.IC_CNT_EVICTIONS],
                           current_fill=sf + rf + imf, sink_fill=sf, recent_fill=rf, important_fill=imf,
-                          total_promotions=n[_lib.IC_CNT_PROMOTIONS])
+                          total_promotions=n[_lib.IC_CNT_PROMOTIONS], near_ties=n[_lib.IC_CNT_NEAR_TIES])
 
     def stats(self, session: int) -> CacheStats:
         return self._stats_from(self.ctrl[session].tolist(), self.counters[session].tolist())

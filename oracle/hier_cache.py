@@ -97,6 +97,7 @@ class OracleCache:
         self.step = 0
         self.total_tokens_seen = 0
         self.total_evictions = 0
+        self.near_ties = 0  # L2 decisions whose two smallest scores were within 1e-6 relative
         self.events: List[Event] = []
 
     @property
@@ -231,6 +232,13 @@ class OracleCache:
             kind, epos = EV_FILL, -1
         else:
             target = self._l2_min_slot()
+            s0 = g.important_start
+            l2 = np.asarray(self.importance[s0:s0 + self.important_fill], np.float32)
+            if l2.shape[0] > 1:
+                lo = np.float32(self.importance[target])
+                runner = np.min(np.delete(l2, target - s0))
+                if float(runner) - float(lo) <= 1e-6 * abs(float(lo)):
+                    self.near_ties += 1
             if not (score > self.importance[target]):
                 return Event(EV_REJECT, dpos, target, -1)
             kind, epos = EV_EVICT, int(self.positions[target])

@@ -22,7 +22,7 @@ def declared_functions():
 
 def test_library_loads():
     lib = _lib.load()
-    assert lib.ic_abi_version() == 2
+    assert lib.ic_abi_version() == 3
 
 
 def test_exports_every_declared_symbol():

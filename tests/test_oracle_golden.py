@@ -151,3 +151,19 @@ def test_paged_trace(golden):
         assert msc.alloc.free == json.loads(str(g["free"][i])), (i, op)
         assert abs(msc.alloc.utilization() - float(g["util"][i])) < 1e-12
     assert np.array_equal(np.concatenate(gathers), g["gathers"])
+
+
+def test_torch_fp32_mass_matches_oracle():
+    """The torch fp32 restatement of the attention mass used at full size on
+    the GPU agrees with the oracle (which is pinned to the reference's
+    fixture above) on a 1024-token, 16/2-head case."""
+    import torch
+    from mass_reference import attention_mass_fp32
+    from oracle.summary import attention_mass
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(16, 1024, 128, generator=g).bfloat16().float()
+    k = torch.randn(2, 1024, 128, generator=g).bfloat16().float()
+    cs_t, imp_t = attention_mass_fp32(q, k, chunk=256)
+    cs_o, imp_o = attention_mass(q.numpy(), k.numpy())
+    assert np.allclose(cs_t.numpy(), cs_o, rtol=2e-6, atol=0)
+    assert np.allclose(imp_t.numpy(), imp_o, rtol=2e-6, atol=0)

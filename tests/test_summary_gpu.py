@@ -170,6 +170,61 @@ def test_summary_full_size_properties():
     assert abs(float(p.sum(dim=1)[0]) - float(res.head_mass[0, 0, j])) <= 1e-3 * float(res.head_mass[0, 0, j])
 
 
+def test_config4_retained_set_full_size():
+    """Config 4 at full size -- 8 sequences x 16/2 heads x 8192 tokens, bf16,
+    q / k / v ~ N(0, 1) from seed 3 -- through the path the two-pass engine
+    runs: kernel C's importance, then kernel D's 4/256/780 tier fill into a
+    cache.  The reference retained set is the oracle's tier fill of the fp32
+    attention mass of the same bf16-rounded q / k (the oracle's formula in
+    torch fp32, tests/mass_reference.py, itself checked against the oracle on
+    the CPU).
+
+    The bar: the GPU importance is within IMP_RTOL relative of the fp32 mass
+    for every token, and a token may sit in one set and not the other only if
+    its fp32 mass lies within 2 x the largest observed relative error of the
+    reference set's cut (the smallest retained importance-tier score): such a
+    token's order against the cut is decided below the kernel's rounding.
+    Both the counts and the distances are printed."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    from infercache_b200.summary import summary_score
+    from mass_reference import attention_mass_fp32
+    B, Hq, Hkv, T, D = 8, 16, 2, 8192, 128
+    sink, recent, important = 4, 256, 780
+    IMP_RTOL = 1e-4
+    q, k, v = rand_qkv(B, Hq, Hkv, T, torch.bfloat16, seed=3)
+    res = summary_score(q, k, v)
+    imp_gpu = res.importance
+    cfg = CacheConfig(num_layers=1, num_kv_heads=Hkv, head_dim=D, sink_size=sink, recent_size=recent,
+                      important_size=important, dtype=torch.bfloat16)
+    cache = SessionBatch(cfg, B, "cuda:0")
+    for b in range(B):
+        cache.load_prompt(b, ((k[b][None], v[b][None]),), imp_gpu[b])
+    pos_gpu = cache.positions.cpu().numpy()
+    occ_gpu = cache.occupied.cpu().numpy()
+    report = []
+    for b in range(B):
+        _, imp_ref = attention_mass_fp32(q[b], k[b])
+        ref = imp_ref.cpu().numpy()
+        got = imp_gpu[b].cpu().numpy()
+        err = float(np.max(np.abs(got - ref) / ref))
+        assert err <= IMP_RTOL, (b, err)
+        tf = tier_fill(ref, None, sink, recent, important)
+        sel_ref = set(tf["slot_token"][tf["occupied"]].tolist())
+        sel_gpu = set(pos_gpu[b][occ_gpu[b]].tolist())
+        assert len(sel_gpu) == len(sel_ref) == sink + recent + important
+        l2_ref = [t for t in sel_ref if sink <= t < T - recent]
+        cut = float(np.min(ref[l2_ref]))
+        diff = sorted(sel_gpu ^ sel_ref)
+        dist = [abs(float(ref[t]) - cut) / cut for t in diff]
+        report.append((b, len(diff), err, max(dist) if dist else 0.0))
+        for t, d in zip(diff, dist):
+            assert sink <= t < T - recent, (b, t)          # sinks and the recent tail always agree
+            assert d <= 2 * err, (b, t, d, err)
+    print("config-4 retained sets (sequence, tokens differing, max importance rel err, max distance from cut):",
+          report)
+    cache.check_device_status()
+
+
 def test_summary_rejects_bad_args():
     from infercache_b200 import _lib
     from infercache_b200.summary import summary_score
