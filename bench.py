@@ -482,6 +482,147 @@ def config3_leg(device, steps=20, warmup=3):
                          "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
 
 
+MODEL_WORKLOAD = dict(layers=36, hidden=2048, hq=16, hkv=2, d=128, intermediate=11008, vocab=151936,
+                      sessions=16, prompt=2048, steps=512, seed=1)
+
+
+def model_leg(device, steps=None, ref_steps=16):
+    """Config 2 with its model: a Qwen2.5-3B-shaped decoder (36 layers, hidden
+    2048, 16/2 heads, intermediate 11008, vocab 151936, tied embeddings) with
+    random-init fp16 weights (normal(0, 0.02), seed 1); 16 sessions, each a
+    2048-token random prompt (seed 1) prefilled with kernel C as the attention
+    (received mass of the last layer, the two-pass engine's attention-mass
+    mode) and primed into a 4/256/780 budget by kernel D; then greedy decode of
+    all 16 sessions as one batch, kernel A (one layer at a time) as each
+    layer's attention and kernel B after each forward.  Weight GEMMs are
+    cuBLAS through the model.  Timed: the decode steps eagerly, the same step
+    captured as one CUDA graph, and the reference's loop on the same GPU
+    (per step: every session's retained K/V exported in position order into a
+    DynamicCache, the model with SDPA, push of the new token without weights,
+    two_pass.py:302-336)."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    from infercache_b200 import CacheConfig, SessionBatch, hf_attention
+    from infercache_b200.cache_safety import normalise_kv, to_dynamic_cache
+    w = MODEL_WORKLOAD
+    S, L, T = w["sessions"], w["layers"], w["prompt"]
+    steps = steps or w["steps"]
+    mcfg = Qwen2Config(vocab_size=w["vocab"], hidden_size=w["hidden"], intermediate_size=w["intermediate"],
+                       num_hidden_layers=L, num_attention_heads=w["hq"], num_key_value_heads=w["hkv"],
+                       max_position_embeddings=32768, rms_norm_eps=1e-6, tie_word_embeddings=True,
+                       rope_parameters={"rope_theta": 1000000.0, "rope_type": "default"}, initializer_range=0.02)
+    torch.manual_seed(w["seed"])
+    t0 = time.perf_counter()
+    with torch.device(device):
+        model = Qwen2ForCausalLM._from_config(mcfg, dtype=torch.float16)
+    model.eval()
+    n_params = sum(p.numel() for p in model.parameters())
+    build_s = time.perf_counter() - t0
+    ccfg = CacheConfig(num_layers=L, num_kv_heads=w["hkv"], head_dim=w["d"], sink_size=4, recent_size=256,
+                       important_size=780, decay=0.99, dtype=torch.float16)
+    b = SessionBatch(ccfg, S, device)
+    g = torch.Generator().manual_seed(w["seed"])
+    prompts = torch.randint(0, w["vocab"], (S, T), generator=g)
+    first = []
+    t0 = time.perf_counter()
+    with torch.inference_mode():
+        for s_ in range(S):
+            ctx = hf_attention.SummaryContext(L, all_layers=False, layer_idx=-1)
+            with hf_attention.active(model, ctx):
+                out = model(prompts[s_:s_ + 1].to(device), use_cache=True, logits_to_keep=1)
+            b.load_prompt(s_, out.past_key_values, ctx.importance())
+            first.append(int(out.logits[0, -1].argmax()))
+            del out
+    torch.cuda.synchronize()
+    prime_s = time.perf_counter() - t0
+    tok = torch.tensor(first, device=device, dtype=torch.long).view(S, 1)
+    pos = torch.full((S,), T, dtype=torch.int64, device=device)
+    dctx = hf_attention.DecodeContext(b)
+    pcache = hf_attention.pass_through_cache()
+
+    def step():
+        with hf_attention.active(model, dctx):
+            out = model(tok, position_ids=pos.view(S, 1), past_key_values=pcache, use_cache=True, logits_to_keep=1)
+        b.evict(pos)
+        tok.copy_(out.logits[:, -1].argmax(-1).view(S, 1))
+        pos.add_(1)
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    res = {"workload": f"qwen2.5-3b-shaped decoder ({n_params / 1e9:.2f} B params, random-init fp16), {S} sessions x "
+                       f"{T}-token random prompts (seed {w['seed']}), budget 4/256/780, greedy decode",
+           "params": n_params, "model_build_s": build_s, "prefill_and_prime_s": prime_s}
+    with torch.inference_mode():
+        for _ in range(4):
+            step()
+        ms_eager = timed(step, min(steps, 64))
+        res["eager"] = {"ms_per_step": ms_eager, "value": S / (ms_eager / 1e3), "steps": min(steps, 64)}
+        try:
+            cap = torch.cuda.Stream()
+            cap.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=cap):
+                step()
+            for _ in range(3):
+                graph.replay()
+            ms_graph = timed(graph.replay, steps)
+            res["cuda_graph"] = {"ms_per_step": ms_graph, "value": S / (ms_graph / 1e3), "steps": steps}
+            del graph
+        except Exception as e:  # report; the eager figure stands
+            res["cuda_graph"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        b.check_device_status()
+        # attention's share: the 36 kernel-A launches of one step alone
+        q = torch.randn(L, S, w["hq"], w["d"], device=device, dtype=torch.float16)
+        kv = torch.randn(L, S, w["hkv"], w["d"], device=device, dtype=torch.float16)
+        o = torch.empty_like(q)
+
+        def attn_only():
+            for l in range(L):
+                b.attend(l, q[l], kv[l], kv[l], out=o[l])
+            b.evict(pos)
+
+        attn_only()
+        ms_attn = timed(attn_only, 32)
+        res["attention_ms_per_step"] = ms_attn
+        best = res.get("cuda_graph", {}).get("ms_per_step") or ms_eager
+        res["attention_share"] = ms_attn / best
+
+        # the reference's loop on the same GPU
+        def ref_step():
+            Ks, Vs = zip(*[b.gather(s_) for s_ in range(S)])
+            K = torch.stack(Ks, 1)
+            V = torch.stack(Vs, 1)
+            dc = to_dynamic_cache([(K[l], V[l]) for l in range(L)])
+            out = model(tok, position_ids=pos.view(S, 1), past_key_values=dc, use_cache=True, logits_to_keep=1)
+            new = normalise_kv(out.past_key_values)
+            nk = torch.stack([new[l][0][:, :, -1] for l in range(L)], 1)  # [S, L, Hkv, D]
+            nv = torch.stack([new[l][1][:, :, -1] for l in range(L)], 1)
+            p_host = pos.tolist()
+            for s_ in range(S):
+                b.push(s_, nk[s_][:, :, None], nv[s_][:, :, None], p_host[s_])
+            tok.copy_(out.logits[:, -1].argmax(-1).view(S, 1))
+            pos.add_(1)
+
+        ref_step()
+        ms_ref = timed(ref_step, ref_steps)
+        res["reference_loop_same_gpu"] = {"ms_per_step": ms_ref, "value": S / (ms_ref / 1e3), "steps": ref_steps}
+    b.check_device_status()
+    best_v = max(v.get("value", 0.0) for v in (res["eager"], res.get("cuda_graph", {})))
+    res["value"] = best_v
+    res["unit"] = "session-tokens/s"
+    res["vs_reference_loop"] = best_v / res["reference_loop_same_gpu"]["value"]
+    del model, b
+    torch.cuda.empty_cache()
+    return res
+
+
 # ---- our arm ----------------------------------------------------------------------------------
 def build_batch(spec, device, seed):
     from infercache_b200 import CacheConfig, SessionBatch
@@ -519,7 +660,7 @@ def main():
                          "the spread)")
     ap.add_argument("--no-summary", action="store_true",
                     help="skip the secondary legs (summary scorer, paged gather, 7B-shaped decode, graph cache)")
-    ap.add_argument("--workload", choices=["decode", "summary", "graph"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "summary", "graph", "model"], default="decode",
                     help="summary / graph: time only the summary-pass scorer / the graph cache (for profiling)")
     ap.add_argument("--summary-batch", type=int, default=0, help="sequences in the summary workload")
     args = ap.parse_args()
@@ -537,6 +678,10 @@ def main():
     if args.workload == "summary":
         if rank == 0:
             print(json.dumps(summary_leg(device, iters=args.steps, batch=args.summary_batch or None)), flush=True)
+        return
+    if args.workload == "model":
+        if rank == 0:
+            print(json.dumps(model_leg(device, steps=args.steps)), flush=True)
         return
     if args.workload == "graph":
         if rank == 0:
@@ -734,7 +879,7 @@ def main():
     h2d, d2h = stepper.h2d_bytes, stepper.d2h_bytes
     b.check_device_status()
 
-    summ = paged = c3 = graph = None
+    summ = paged = c3 = graph = model = None
     # the secondary legs and CPU baselines are per-GPU figures: one GPU runs them
     if not args.no_summary and world == 1:
         log("summary leg")
@@ -743,6 +888,8 @@ def main():
         paged = paged_leg(device)
         log("7b-shaped decode leg")
         c3 = config3_leg(device)
+        log("model leg")
+        model = model_leg(device)
         log("graph cache leg")
         graph = graph_leg(device, cpu_sample=256 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0)
 
@@ -793,7 +940,8 @@ def main():
                 "summary_score": summ,
                 "paged_gather": paged,
                 "decode_7b_shape": c3,
-                "graph_cache": graph}
+                "graph_cache": graph,
+                "model_decode_3b": model}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphs
