@@ -425,21 +425,27 @@ C3_WORKLOAD = dict(layers=28, hq=28, hkv=4, d=128, sessions=64, min_prompt=1024,
 C3_ALG_BYTES_PER_SESSION_LAYER = 4_227_584  # K/V 4,194,304 + append 2,048 + q/o 14,336 + table 512 + importance 16,384
 
 
-def config3_leg(device, steps=20, warmup=3):
+def config3_leg(device, steps=20, warmup=3, rank=0, world=1, sync=None):
     """The Qwen2.5-7B-shaped decode: 28 layers, 28/4 heads, head_dim 128,
     budget 2048 (4/512/1532), 64 sessions primed from prompts of U[1024, 8192]
     tokens (seed 2), fp16.  A step is one decode step of every session
     (28 layer launches + kernel B per session range); 7.6 GB of K/V per step,
-    far above L2."""
+    far above L2.  With world > 1 the 64 sessions are split contiguously across
+    the ranks (strong scaling) and the time is the max over ranks (`sync`
+    reduces it)."""
     from infercache_b200 import CacheConfig, SessionBatch
     w = C3_WORKLOAD
-    L, Hq, Hkv, D, S = w["layers"], w["hq"], w["hkv"], w["d"], w["sessions"]
+    L, Hq, Hkv, D, S_all = w["layers"], w["hq"], w["hkv"], w["d"], w["sessions"]
+    per = S_all // world
+    mine = range(rank * per, (rank + 1) * per)
+    S = per
     cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=w["sink"], recent_size=w["recent"],
                       important_size=w["important"], decay=w["decay"], dtype=torch.float16)
     b = SessionBatch(cfg, S, device)
     g = torch.Generator().manual_seed(w["seed"])
-    lens = torch.randint(w["min_prompt"], w["max_prompt"] + 1, (S,), generator=g).tolist()
-    gd = torch.Generator(device=device).manual_seed(w["seed"])
+    lens = torch.randint(w["min_prompt"], w["max_prompt"] + 1, (S_all,), generator=g).tolist()
+    lens = [lens[i] for i in mine]
+    gd = torch.Generator(device=device).manual_seed(w["seed"] * 1000 + rank)
     for s_, T in enumerate(lens):
         pk = torch.randn(L, 1, Hkv, T, D, generator=gd, device=device, dtype=torch.float16)
         pv = torch.randn(L, 1, Hkv, T, D, generator=gd, device=device, dtype=torch.float16)
@@ -456,10 +462,12 @@ def config3_leg(device, steps=20, warmup=3):
         pos.add_(1)
     torch.cuda.synchronize()
     # session ranges on their own streams, STEPS_PER_GRAPH steps per graph
-    gs = b.grouped_stepper(q, k, v, out, pos, groups=SESSION_GROUPS, steps_per_graph=STEPS_PER_GRAPH)
+    gs = b.grouped_stepper(q, k, v, out, pos, groups=min(SESSION_GROUPS, S), steps_per_graph=STEPS_PER_GRAPH)
     gs.run(max(1, warmup // STEPS_PER_GRAPH))
     torch.cuda.synchronize()
     reps = max(1, steps // STEPS_PER_GRAPH)
+    if sync is not None:
+        sync(None)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     gs.run(reps)
@@ -467,19 +475,26 @@ def config3_leg(device, steps=20, warmup=3):
     torch.cuda.synchronize()
     b.check_device_status()
     steps = reps * STEPS_PER_GRAPH
-    ms = e0.elapsed_time(e1) / steps
+    ms = e0.elapsed_time(e1)
+    if sync is not None:
+        ms = sync(ms)
+    ms = ms / steps
+    S = S_all if world > 1 else S
     alg = S * L * C3_ALG_BYTES_PER_SESSION_LAYER
     peak, kind = measured_peak()
+    peak *= world  # the aggregate of the ranks' HBM
     gbs = alg / (ms / 1e3) / 1e9
     del gs, b, q, k, v, out
     return {"workload": f"qwen2.5-7b-shaped decode: {S} sessions x {L} layers, {Hq}/{Hkv} heads, head_dim {D}, "
-                        f"budget 2048 (4/512/1532), prompts U[1024, 8192] (seed 2), fp16",
+                        f"budget 2048 (4/512/1532), prompts U[1024, 8192] (seed 2), fp16"
+                        + (f"; strong scaling: {per} sessions on each of {world} GPUs" if world > 1 else ""),
+            "n_gpus": world,
             "value": S / (ms / 1e3), "unit": "session-tokens/s", "ms_per_step": ms, "steps": steps,
             "alg_bytes_per_step": alg,
-            "cuda_graph": f"{STEPS_PER_GRAPH} steps per graph; {SESSION_GROUPS} session ranges of "
-                          f"{S // SESSION_GROUPS} on their own streams and graphs",
+            "cuda_graph": f"{STEPS_PER_GRAPH} steps per graph; {min(SESSION_GROUPS, per)} session ranges per GPU on "
+                          f"their own streams and graphs",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                         "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)"}}
+                         "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs" + (f" x {world} GPUs)" if world > 1 else ")")}}
 
 
 MODEL_WORKLOAD = dict(layers=36, hidden=2048, hq=16, hkv=2, d=128, intermediate=11008, vocab=151936,
@@ -880,6 +895,16 @@ def main():
     b.check_device_status()
 
     summ = paged = c3 = graph = model = None
+    c3_strong = None
+    if world > 1 and not args.no_summary and C3_WORKLOAD["sessions"] % world == 0:
+        # config 3 split across the ranks: the 64 sessions, max time over ranks
+        def sync(x):
+            if x is None:
+                barrier()
+                return None
+            return max_over_ranks(x)
+        log("7b-shaped decode, strong scaling")
+        c3_strong = config3_leg(device, rank=rank, world=world, sync=sync)
     # the secondary legs and CPU baselines are per-GPU figures: one GPU runs them
     if not args.no_summary and world == 1:
         log("summary leg")
@@ -940,6 +965,7 @@ def main():
                 "summary_score": summ,
                 "paged_gather": paged,
                 "decode_7b_shape": c3,
+                "decode_7b_shape_strong": c3_strong,
                 "graph_cache": graph,
                 "model_decode_3b": model}
         print(json.dumps(line), flush=True)
