@@ -524,6 +524,16 @@ int ic_graph_select(const ic_graph_select_args* a, void* stream);
  * IC_ERR_INVALID_ARG when `host` is not page-locked mapped memory. */
 int ic_host_device_pointer(const void* host, void** device);
 
+/* ---- bounded-wait check ------------------------------------------------------
+ * Launches one thread that waits, through the same bounded mbarrier wait every
+ * kernel here uses, for a barrier phase that nothing completes.  After
+ * limit_ns of %globaltimer (at most 2 s) the wait gives up, ORs
+ * IC_DEVFLAG_TIMEOUT into *dev_status and the kernel returns normally, so the
+ * context stays usable.  Lets a caller test its handling of a device-side
+ * timeout (IC_ERR_DEVICE_TIMEOUT) without a real hang.  No reference
+ * counterpart (the reference has no device-side waits). */
+int ic_wait_probe(int32_t* dev_status, int64_t limit_ns, void* stream);
+
 /* ---- library information --------------------------------------------------*/
 const char* ic_status_str(int status);
 int ic_abi_version(void);

@@ -213,7 +213,7 @@ ENTRY_POINTS = {
     "ic_graph_select": ic_graph_select_args,
 }
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
-HOST_ENTRY_POINTS = ["ic_host_device_pointer"]
+HOST_ENTRY_POINTS = ["ic_host_device_pointer", "ic_wait_probe"]
 
 _LIB = None
 
@@ -241,6 +241,8 @@ def load(path: Path = LIB_PATH):
     lib.ic_last_error.restype = c_char_p
     lib.ic_host_device_pointer.argtypes = [c_void_p, POINTER(c_void_p)]
     lib.ic_host_device_pointer.restype = c_int
+    lib.ic_wait_probe.argtypes = [c_void_p, c_int64, c_void_p]
+    lib.ic_wait_probe.restype = c_int
     _LIB = lib
     return lib
 

@@ -73,3 +73,25 @@ extern "C" int ic_device_check(void) {
 }
 
 extern "C" const char* ic_last_error(void) { return ic::g_last_error; }
+
+namespace {
+
+// One thread waits for phase 0 of an mbarrier whose single expected arrival
+// never comes; the bounded wait reports the timeout in *status and returns.
+__global__ void wait_probe_kernel(int32_t* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  ic::mbar_init(&bar, 1);
+  ic::fence_barrier_init();
+  ic::mbar_wait_bounded(&bar, 0, status, limit_ns);
+}
+
+}  // namespace
+
+extern "C" int ic_wait_probe(int32_t* dev_status, int64_t limit_ns, void* stream) {
+  if (!dev_status || limit_ns <= 0 || limit_ns > 2000000000LL) {
+    ic::set_last_error("wait_probe: dev_status required, 0 < limit_ns <= 2e9");
+    return IC_ERR_INVALID_ARG;
+  }
+  wait_probe_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(dev_status, static_cast<uint64_t>(limit_ns));
+  return ic::launch_status("wait_probe");
+}

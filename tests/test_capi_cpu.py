@@ -50,6 +50,15 @@ def test_host_device_pointer_rejects_null_without_cuda_call():
     assert lib.ic_host_device_pointer(None, ctypes.byref(out)) == _lib.IC_ERR_INVALID_ARG
 
 
+def test_wait_probe_rejects_bad_args_without_cuda_call():
+    lib = _lib.load()
+    assert lib.ic_wait_probe(None, 1000, None) == _lib.IC_ERR_INVALID_ARG
+    import ctypes
+    x = ctypes.c_int32(0)
+    assert lib.ic_wait_probe(ctypes.addressof(x), 0, None) == _lib.IC_ERR_INVALID_ARG
+    assert lib.ic_wait_probe(ctypes.addressof(x), 3_000_000_000, None) == _lib.IC_ERR_INVALID_ARG
+
+
 def test_null_args_rejected_without_launch():
     """Argument validation runs on the host before any CUDA call."""
     lib = _lib.load()

@@ -699,3 +699,33 @@ def test_attend_split_kernel_small(dtype, hq, variant):
     sp.update(hq=hq, hkv=2)
     cache, oc, outs, events = run_small_attend(sp, dtype, variant)
     cache.batch.check_device_status()
+
+
+def test_device_timeout_is_reported_and_context_survives():
+    """A bounded device-side wait that runs out (ic_wait_probe: an mbarrier
+    phase nothing completes, 50 ms limit) sets IC_DEVFLAG_TIMEOUT; the host
+    maps it to IC_ERR_DEVICE_TIMEOUT; the context stays usable, so after the
+    flag is cleared the cache decodes and checks clean."""
+    import ctypes
+    from infercache_b200 import _lib
+    cache = make_gpu_cache(2, 2, 128, 2, 5, 4, torch.float16)
+    b = cache.batch
+    lib = _lib.load()
+    rc = lib.ic_wait_probe(ctypes.c_void_p(b.dev_status.data_ptr()), 50_000_000,
+                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == _lib.IC_OK
+    torch.cuda.synchronize()
+    assert int(b.dev_status.item()) & _lib.IC_DEVFLAG_TIMEOUT
+    with pytest.raises(_lib.InferCacheError) as ei:
+        b.check_device_status()
+    assert ei.value.status == _lib.IC_ERR_DEVICE_TIMEOUT
+    b.dev_status.zero_()
+    g = torch.Generator().manual_seed(4)
+    pk = torch.randn(2, 2, 12, 128, generator=g).half()
+    cache.load_from_hf_output(tuple((pk[l][None], pk[l][None]) for l in range(2)), torch.rand(12, generator=g))
+    q = torch.randn(2, 4, 128, generator=g).half().cuda()
+    kv = torch.randn(2, 2, 128, generator=g).half().cuda()
+    o = cache.step(q, kv, kv, 12)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all()
+    b.check_device_status()
