@@ -399,7 +399,9 @@ int ic_summary_score(const ic_summary_args* a, void* stream);
  * All calls share the one array: calls that overlap on the GPU (other
  * streams, other host threads) race and corrupt each other's results; order
  * them on one stream.  No element needs clearing between calls: each call
- * writes every element it reads. */
+ * writes every element it reads.  The outputs are undefined when dev_status
+ * reports an error, and calls after a cudaDeviceReset are not supported (the
+ * array's address is looked up once per device). */
 #define IC_SUMMARY_STATIC_MASS_MAX 4194304
 int ic_summary_score_static(const ic_summary_args* a, void* stream);
 

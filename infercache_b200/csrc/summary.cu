@@ -736,6 +736,11 @@ extern "C" int ic_summary_score(const ic_summary_args* a, void* stream) {
 // 4. ic_summary_score_static: the scorer with its per-head mass in a library-owned
 //    static device array, for callers that cannot allocate device memory
 // ------------------------------------------------------------------------------
+// The array's address is looked up once per device and kept: after a
+// cudaDeviceReset (or any teardown of the primary context) the module is
+// loaded again and the cached address is stale, so calls after a device reset
+// are not supported.
+//
 // Some callers cannot hand this library a scratch buffer: code that runs
 // while another allocator owns all of the GPU's free memory (a serving
 // process that reserved it up front), or a binding from a language with no
@@ -805,7 +810,9 @@ extern "C" int ic_summary_score_static(const ic_summary_args* a, void* stream) {
   const int rc = scratch_address(&scratch);
   if (rc != IC_OK) return rc;
   // every element of the mass that the column sum reads is written earlier in
-  // the same call, so the array needs no clearing between calls
+  // the same call, so the array needs no clearing between calls -- except after
+  // a bounded wait gave up (dev_status reports IC_DEVFLAG_TIMEOUT): the forward
+  // kernel then skips its stores and the outputs are undefined
   ic_summary_args b = *a;
   b.head_mass = scratch;
   return ic_summary_score(&b, stream);

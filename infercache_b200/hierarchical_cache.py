@@ -569,7 +569,8 @@ class GroupedStepper:
         cap.wait_stream(torch.cuda.current_stream(dev))
         for a in self._args:
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
+            # relaxed: a kernel's first launch may set its shared-memory attribute
+            with torch.cuda.graph(g, stream=cap, capture_error_mode="relaxed"):
                 for _ in range(self.steps_per_graph):
                     _lib.call("ic_decode_step", a)
             self.graphs.append(g)

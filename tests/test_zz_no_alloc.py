@@ -41,24 +41,39 @@ def test_rejects_before_any_cuda_call():
     assert b"static scratch" in lib.ic_last_error() or b"bad shape" in lib.ic_last_error()
 
 
-def _run(name, q, k, v, with_head_mass):
+def _run(name, q, k, v, with_head_mass, with_out=True, colsum0=None):
+    """One call; colsum0 (if given) pre-fills colsum and sets accumulate."""
     B, Hq, T, D = q.shape
     dev = q.device
-    out = torch.empty_like(q)
+    out = torch.empty_like(q) if with_out else None
     lse = torch.empty(B, Hq, T, dtype=torch.float32, device=dev)
     hm = torch.empty(B, Hq, T, dtype=torch.float32, device=dev) if with_head_mass else None
-    colsum = torch.empty(B, T, dtype=torch.float32, device=dev)
+    colsum = colsum0.clone() if colsum0 is not None else torch.empty(B, T, dtype=torch.float32, device=dev)
     imp = torch.empty(B, T, dtype=torch.float32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    a = _lib.ic_summary_args(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr(),
-                             lse=lse.data_ptr(), head_mass=_lib.ptr(hm), colsum=colsum.data_ptr(),
+    a = _lib.ic_summary_args(q=q.data_ptr(), k=k.data_ptr(), v=_lib.ptr(v if with_out else None),
+                             out=_lib.ptr(out), lse=lse.data_ptr(), head_mass=_lib.ptr(hm), colsum=colsum.data_ptr(),
                              importance=imp.data_ptr(), batch=B, num_q_heads=Hq, num_kv_heads=k.shape[1],
-                             seq_len=T, head_dim=D, dtype=_lib.dtype_code(q.dtype), accumulate=0,
-                             scale=D ** -0.5, dev_status=status.data_ptr())
+                             seq_len=T, head_dim=D, dtype=_lib.dtype_code(q.dtype),
+                             accumulate=1 if colsum0 is not None else 0, scale=D ** -0.5,
+                             dev_status=status.data_ptr())
     _lib.call(name, a)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     return out, lse, colsum, imp
+
+
+def _compare(ref, got):
+    if ref[0] is not None:
+        o_ref, o_got = ref[0].float().cpu().numpy(), got[0].float().cpu().numpy()
+        assert np.abs(o_got - o_ref).max() <= 1e-5 * np.abs(o_ref).max()
+    for r, x in zip(ref[1:], got[1:]):
+        assert elem_close(x.cpu().numpy(), r.cpu().numpy(), 1e-5)
+
+
+def _inputs(seed, B, Hq, Hkv, T, dtype):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return tuple(torch.randn(B, H, T, 128, generator=g, device="cuda").to(dtype) for H in (Hq, Hkv, Hkv))
 
 
 @pytest.mark.gpu
@@ -79,3 +94,33 @@ def test_static_scratch_matches_caller_buffer_twice():
         assert np.abs(o_got - o_ref).max() <= 1e-5 * np.abs(o_ref).max()
         for r, x in zip(ref[1:], got[1:]):
             assert elem_close(x.cpu().numpy(), r.cpu().numpy(), 1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["fp16", "no_output", "accumulate", "at_limit"])
+def test_static_scratch_variants(case):
+    """The other argument forms against ic_summary_score with a caller
+    head_mass: fp16 inputs; no attention output (out and v NULL); colsum
+    accumulated onto a pre-filled buffer (the all-layers sum); and a shape
+    exactly at the limit (batch * heads * seq_len == IC_SUMMARY_STATIC_MASS_MAX)."""
+    _lib.require_device(torch.device("cuda", 0))
+    torch.cuda.set_device(0)
+    if case == "fp16":
+        q, k, v = _inputs(51, 2, 16, 2, 640, torch.float16)
+        ref, got = _run("ic_summary_score", q, k, v, True), _run("ic_summary_score_static", q, k, v, False)
+    elif case == "no_output":
+        q, k, v = _inputs(52, 1, 16, 2, 900, torch.bfloat16)
+        ref = _run("ic_summary_score", q, k, v, True, with_out=False)
+        got = _run("ic_summary_score_static", q, k, v, False, with_out=False)
+    elif case == "accumulate":
+        q, k, v = _inputs(53, 2, 8, 1, 500, torch.bfloat16)
+        c0 = torch.rand(2, 500, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda")
+        ref = _run("ic_summary_score", q, k, v, True, colsum0=c0)
+        got = _run("ic_summary_score_static", q, k, v, False, colsum0=c0)
+    else:
+        T = _lib.IC_SUMMARY_STATIC_MASS_MAX // 16 // 2
+        q, k, v = _inputs(54, 2, 16, 2, T, torch.bfloat16)
+        assert q.shape[0] * q.shape[1] * q.shape[2] == _lib.IC_SUMMARY_STATIC_MASS_MAX
+        ref = _run("ic_summary_score", q, k, v, True, with_out=False)
+        got = _run("ic_summary_score_static", q, k, v, False, with_out=False)
+    _compare(ref, got)
