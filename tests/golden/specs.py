@@ -167,3 +167,45 @@ def graph_inputs(name):
     qdir = torch.randint(0, sp["n_dirs"], (nq,), generator=g)
     queries = dirs[qdir][:, None, :] * 3.0 + torch.randn(nq, H, D, generator=g) * 0.8
     return k.half(), v.half(), scores, queries
+
+
+# Two-pass engine comparator: a tiny random-weight Qwen2-shaped decoder
+# (head_dim 128) built on the CPU from a seed, a deterministic character
+# tokenizer, a 300-character prompt (two-pass path: longer than the summary
+# threshold) and a 4/16/40 budget so tokens are evicted while decoding.
+TWOPASS = dict(seed=1, layers=3, sink=4, recent=16, important=40, max_new_tokens=48, vocab=512)
+
+
+class CharTokenizer:
+    eos_token_id = None
+    unk_token_id = 0
+
+    def __init__(self, vocab=512):
+        self.vocab = vocab
+        self.vocab_size = vocab
+
+    def encode(self, text, return_tensors=None, add_special_tokens=False):
+        ids = [(ord(c) * 7) % self.vocab for c in text]
+        return torch.tensor([ids]) if return_tensors == "pt" else ids
+
+    def decode(self, ids, skip_special_tokens=False):
+        return "".join(chr(32 + int(i) % 90) for i in ids)
+
+
+def tiny_qwen2(seed=0, layers=3, vocab=512):
+    """fp32 on the CPU; q / k projections scaled up so attention is peaked."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    cfg = Qwen2Config(vocab_size=vocab, hidden_size=256, intermediate_size=512, num_hidden_layers=layers,
+                      num_attention_heads=2, num_key_value_heads=1, max_position_embeddings=4096,
+                      rope_theta=10000.0, tie_word_embeddings=True)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    m = Qwen2ForCausalLM(cfg)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if ("q_proj" in n or "k_proj" in n) and p.dim() == 2:
+                p.mul_(4.0)
+    return m.eval()
+
+
+TWOPASS_PROMPT = "".join(chr(33 + (i * 37) % 90) for i in range(300))

@@ -11,7 +11,10 @@ Qwen2-shaped model (head_dim 128), on a B200.
 * fused decode (kernel A as the model's attention + kernel B) against the
   reference's DynamicCache loop: identical greedy tokens and identical cache
   state (fp32 model, exact index work);
-* the short-prompt direct path against a plain Hugging Face greedy loop.
+* the short-prompt direct path against a plain Hugging Face greedy loop;
+* both decode paths against the reference's own TwoPassEngine (fixture made
+  by running it on the CPU), and the memory engine's save / load calls on the
+  cache against the oracle.
 """
 import numpy as np
 import pytest
@@ -21,33 +24,12 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-class CharTokenizer:
-    eos_token_id = None
-
-    def __init__(self, vocab):
-        self.vocab = vocab
-
-    def encode(self, text, return_tensors=None):
-        ids = [(ord(c) * 7) % self.vocab for c in text]
-        return torch.tensor([ids]) if return_tensors == "pt" else ids
-
-    def decode(self, ids, skip_special_tokens=False):
-        return "".join(chr(32 + int(i) % 90) for i in ids)
+from specs import CharTokenizer, tiny_qwen2
 
 
 def tiny_model(dtype, seed=0, layers=3):
-    from transformers import Qwen2Config, Qwen2ForCausalLM
-    cfg = Qwen2Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=layers,
-                      num_attention_heads=2, num_key_value_heads=1, max_position_embeddings=4096,
-                      rope_theta=10000.0, tie_word_embeddings=True)
-    cfg._attn_implementation = "sdpa"
-    torch.manual_seed(seed)
-    m = Qwen2ForCausalLM(cfg)
-    with torch.no_grad():  # larger q / k so attention is peaked, not near-uniform
-        for n, p in m.named_parameters():
-            if ("q_proj" in n or "k_proj" in n) and p.dim() == 2:
-                p.mul_(4.0)
-    return m.to("cuda", dtype).eval()
+    """specs.tiny_qwen2 (built on the CPU from the seed) on the GPU in `dtype`."""
+    return tiny_qwen2(seed, layers).to("cuda", dtype).eval()
 
 
 def cache_cfg(model, dtype, sink=4, recent=16, important=40):
@@ -160,3 +142,82 @@ def test_direct_path_matches_plain_loop():
             want.append(nxt)
             past, cur = o.past_key_values, torch.tensor([[nxt]], device="cuda")
     assert got == want
+
+
+@pytest.mark.parametrize("path", ["fused", "dynamic_cache"])
+def test_matches_reference_two_pass_engine(golden, path):
+    """Against the reference's own TwoPassEngine (fixture twopass_ref.npz, made
+    by running it on the CPU: tests/golden/make_twopass_golden.py): the same
+    tiny fp32 model (weights regenerated from the seed), prompt, budget and
+    greedy sampling give the same 48 tokens, the same final slots, positions
+    and eviction count, and importance within 1e-5 (the fixture's smallest
+    top-2 logit margin, ~1e-2, is far above the fp32 differences between the
+    two devices)."""
+    import specs
+    from infercache_b200 import CacheConfig
+    from infercache_b200.two_pass import TwoPassConfig, TwoPassEngine
+    g = golden("twopass_ref")
+    sp = specs.TWOPASS
+    model = specs.tiny_qwen2(sp["seed"], sp["layers"], sp["vocab"]).to("cuda")
+    ccfg = CacheConfig(num_layers=sp["layers"], num_kv_heads=1, head_dim=128, sink_size=sp["sink"],
+                       recent_size=sp["recent"], important_size=sp["important"], dtype=torch.float32)
+    eng = TwoPassEngine(model, specs.CharTokenizer(sp["vocab"]), ccfg,
+                        TwoPassConfig(temperature=0.0, max_new_tokens=sp["max_new_tokens"], decode_path=path))
+    ids = eng.generate_ids(specs.TWOPASS_PROMPT)
+    assert ids == g["ids"].tolist()
+    c = eng._cache
+    assert np.array_equal(c.positions.cpu().numpy(), g["positions"])
+    assert np.array_equal(c.occupied.cpu().numpy(), g["occupied"])
+    imp, ref = c.importance.cpu().numpy(), g["importance"]
+    assert np.all(np.abs(imp - ref) <= 1e-5 * np.maximum(np.abs(ref), 1e-30))
+    assert c.stats.total_evictions == int(g["evictions"])
+
+
+def test_memory_engine_save_load_round_trip():
+    """The cache-side calls of the reference's PersistentMemoryEngine
+    (memory_engine.py:406-410, 434-440) on the new cache: after generation the
+    occupied slots' positions and importance are read through the public
+    tensors (occupied.nonzero, positions[idx], importance[idx]); a later turn
+    re-primes a cache from the stored tokens, sorted by position, through
+    load_from_hf_output with explicit, non-contiguous positions.  The primed
+    state must equal the oracle's load of the same tokens."""
+    import specs
+    from infercache_b200 import CacheConfig, HierarchicalKVCache
+    from infercache_b200.two_pass import TwoPassConfig, TwoPassEngine
+    from oracle.hier_cache import OracleCache, TierGeometry
+    sp = specs.TWOPASS
+    model = specs.tiny_qwen2(sp["seed"], sp["layers"], sp["vocab"]).to("cuda")
+    ccfg = CacheConfig(num_layers=sp["layers"], num_kv_heads=1, head_dim=128, sink_size=sp["sink"],
+                       recent_size=sp["recent"], important_size=sp["important"], dtype=torch.float32)
+    eng = TwoPassEngine(model, specs.CharTokenizer(sp["vocab"]), ccfg, TwoPassConfig(temperature=0.0, max_new_tokens=24))
+    eng.generate_ids(specs.TWOPASS_PROMPT)
+    cache = eng._cache
+    # _save_turn: what it reads
+    occ_idx = cache.occupied.nonzero(as_tuple=True)[0]
+    positions = cache.positions[occ_idx].tolist()
+    importances = cache.importance[occ_idx].tolist()
+    assert len(positions) == cache.total_budget and len(set(positions)) == len(positions)
+    # keep the tokens above a threshold, as min_importance does, then the load path
+    keep = [(p, i) for p, i in zip(positions, importances) if i >= 1e-4] or list(zip(positions, importances))
+    keep.sort(key=lambda r: r[0])
+    pos = [p for p, _ in keep]
+    imp = [i for _, i in keep]
+    g = torch.Generator().manual_seed(8)
+    L, n = sp["layers"], len(pos)
+    k = torch.randn(L, 1, n, 128, generator=g)
+    v = torch.randn(L, 1, n, 128, generator=g)
+    fresh = HierarchicalKVCache(ccfg, device="cuda")
+    fresh.load_from_hf_output(tuple((k[l][None], v[l][None]) for l in range(L)),
+                              importance_scores=torch.tensor(imp, dtype=torch.float32),
+                              positions=torch.tensor(pos, dtype=torch.long))
+    oc = OracleCache(TierGeometry(L, 1, 128, sp["sink"], sp["recent"], sp["important"]), np.float32)
+    oc.load_from_hf_output(k.numpy(), v.numpy(), np.array(imp, np.float32), positions=np.array(pos, np.int64))
+    assert np.array_equal(fresh.positions.cpu().numpy(), oc.positions)
+    assert np.array_equal(fresh.occupied.cpu().numpy(), oc.occupied)
+    assert np.array_equal(fresh.importance.cpu().numpy(), oc.importance)
+    K, V = fresh.K.cpu().numpy(), fresh.V.cpu().numpy()
+    occ = oc.occupied
+    assert np.array_equal(K[:, :, occ], oc.K[:, :, occ]) and np.array_equal(V[:, :, occ], oc.V[:, :, occ])
+    # and the saved state of the restored cache reads back the same way
+    idx2 = fresh.occupied.nonzero(as_tuple=True)[0]
+    assert sorted(fresh.positions[idx2].tolist()) == sorted(oc.positions[occ].tolist())
