@@ -8,8 +8,9 @@ character tokenizer and greedy sampling, in its default hidden-state
 importance mode: summary pass, cache priming (load_from_hf_output), then the
 decode loop (to_hf_past_key_values, model forward, push of the new token).
 Stores the generated token ids, the cache's final positions / occupancy /
-importance and eviction count, and each step's margin between the two largest
-logits (so a test can see how far every greedy choice is from a tie).
+importance and eviction count, each step's margin between the two largest
+logits (so a test can see how far every greedy choice is from a tie), and the
+summary pass's importance scores with the slot layout they primed.
 """
 from __future__ import annotations
 
@@ -50,11 +51,21 @@ def main():
         return orig(logits, generated)
 
     eng._sample = sample
+    primed = {}
+    orig_prime = eng._prime_cache
+
+    def prime(summary):
+        orig_prime(summary)
+        primed["scores"] = summary.importance_scores.numpy().copy()
+        primed["positions"] = eng._cache.positions.numpy().copy()
+
+    eng._prime_cache = prime
     ids = eng.generate_ids(specs.TWOPASS_PROMPT)
     c = eng._cache
     out = dict(ids=np.array(ids, np.int64), positions=c.positions.numpy().copy(),
                occupied=c.occupied.numpy().copy(), importance=c.importance.numpy().copy(),
-               evictions=np.array(c._stats.total_evictions, np.int64), margins=np.array(margins, np.float32))
+               evictions=np.array(c._stats.total_evictions, np.int64), margins=np.array(margins, np.float32),
+               prime_scores=primed["scores"], prime_positions=primed["positions"])
     np.savez_compressed(HERE / "twopass_ref.npz", **out)
     print("tokens", len(ids), "evictions", int(out["evictions"]), "min logit margin", float(min(margins)))
 
