@@ -497,6 +497,225 @@ def config3_leg(device, steps=20, warmup=3, rank=0, world=1, sync=None):
                          "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs" + (f" x {world} GPUs)" if world > 1 else ")")}}
 
 
+C5_WORKLOAD = dict(sessions=512, min_len=256, max_len=32768, seed=4, mean_gap_ms=5.0, decode_steps=64,
+                   layers=36, heads=2, d=128, pool_gb=150.0)
+
+
+def c5_trace(world=1, rank=0):
+    """The config-5 arrivals: session lengths U[256, 32768] and Poisson
+    arrival times (exponential gaps, mean 5 ms), both from seed 4; session i
+    belongs to rank i % world."""
+    w = C5_WORKLOAD
+    g = torch.Generator().manual_seed(w["seed"])
+    lens = torch.randint(w["min_len"], w["max_len"] + 1, (w["sessions"],), generator=g).tolist()
+    gaps = torch.empty(w["sessions"], dtype=torch.float64).exponential_(1.0 / w["mean_gap_ms"], generator=g)
+    arrive = torch.cumsum(gaps, 0).tolist()
+    mine = [i for i in range(w["sessions"]) if i % world == rank]
+    return [(i, lens[i], arrive[i]) for i in mine]
+
+
+def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1.0):
+    """Sessions arrive (simulated clock, ms), are written into the paged pool
+    (PagedSessionView.push of their prompt), then decode `decode_steps` tokens
+    -- per step one token pushed and the session's whole page list gathered
+    into HF layout (to_hf_past_key_values, paged_cache.py:365-378) -- and
+    depart (reset).  A tick serves every active session once; its duration is
+    `tick_timer(fn)` (device time around fn) and advances the clock.  When the
+    pool runs out, the allocator evicts the least recently used session; a
+    session that lost its pages that way is dropped.  Returns counters and the
+    fragmentation sampled every `sample_ms` of simulated time."""
+    pending = sorted(trace, key=lambda x: x[2])
+    active = {}  # sid -> [view, steps_left, n_prompt]
+    now = 0.0
+    busy = 0.0
+    decode_tokens = 0
+    gathered = 0
+    prompt_tokens = 0
+    dropped = 0
+    frag, next_sample = [], 0.0
+    peak_active = 0
+    alloc = msc.allocator
+    tok_k, tok_v = src_k[:, :, :1], src_v[:, :, :1]
+
+    def admit(sid, n):
+        nonlocal prompt_tokens
+        view = msc.get_or_create(str(sid))
+        try:
+            view.push(src_k[:, :, :n], src_v[:, :, :n], positions=[], importance=[])
+        except RuntimeError:
+            pass  # the per-session cap: the tokens that fit are kept, as the reference does
+        active[sid] = [view, decode_steps, n]
+        prompt_tokens += view.n_tokens
+
+    def prune():
+        nonlocal dropped
+        for sid in [k for k, a in active.items() if not alloc.pages_for(str(k))]:
+            msc.reset(str(sid))
+            del active[sid]
+            dropped += 1
+
+    while pending or active:
+        arrivals = []
+        while pending and pending[0][2] <= now:
+            arrivals.append(pending.pop(0))
+        if not active and not arrivals:
+            now = pending[0][2]
+            continue
+        counts = {"decode": 0, "gathered": 0}
+
+        def tick():
+            for sid, n, _ in arrivals:
+                admit(sid, n)
+            prune()
+            for sid in list(active):
+                view = active[sid][0]
+                try:
+                    view.push(tok_k, tok_v, positions=[], importance=[])
+                except RuntimeError:
+                    pass  # at the cap the session decodes over what it holds
+                if not alloc.pages_for(str(sid)):
+                    continue
+                K, V = view.gather_all()
+                counts["decode"] += 1
+                counts["gathered"] += K.numel() * K.element_size() * 2
+                active[sid][1] -= 1
+            prune()
+
+        dt = tick_timer(tick)
+        busy += dt
+        now += dt
+        decode_tokens += counts["decode"]
+        gathered += counts["gathered"]
+        peak_active = max(peak_active, len(active))
+        while next_sample <= now:
+            frag.append(alloc.fragmentation())
+            next_sample += sample_ms
+        for sid in [k for k, a in active.items() if a[1] <= 0]:
+            msc.reset(str(sid))
+            del active[sid]
+    return {"sim_ms": now, "busy_ms": busy, "decode_tokens": decode_tokens, "gathered_bytes": gathered,
+            "prompt_tokens": prompt_tokens, "dropped_by_lru": dropped, "lru_evictions": alloc.lru_evictions,
+            "peak_active": peak_active, "fragmentation_mean": sum(frag) / max(1, len(frag)),
+            "fragmentation_max": max(frag) if frag else 0.0, "fragmentation_samples": len(frag)}
+
+
+class _RecordingAllocator:
+    """Wraps a KVAllocator and records its calls, so the same trace can be
+    replayed through the oracle's allocator afterwards."""
+
+    def __init__(self, inner):
+        self.inner = inner
+        self.ops = []
+
+    def __getattr__(self, name):
+        return getattr(self.inner, name)
+
+    def allocate_pages(self, sid, count):
+        got, err = self.inner.allocate_pages(sid, count)
+        self.ops.append(("alloc", sid, count, tuple(got), str(err) if err else ""))
+        return got, err
+
+    def allocate_page(self, sid):
+        got, err = self.allocate_pages(sid, 1)
+        if err is not None:
+            raise err
+        return got[0]
+
+    def touch(self, sid):
+        self.ops.append(("touch", sid))
+        self.inner.touch(sid)
+
+    def release_session(self, sid):
+        self.ops.append(("release", sid))
+        self.inner.release_session(sid)
+
+
+def replay_on_oracle(ops, n_pages, cap, final_free):
+    """The recorded trace through the oracle's restatement of the reference
+    allocator (paged_cache.py:205-288): every page id, error and the final
+    free list must agree."""
+    from oracle.paged import OracleAllocator
+    oa = OracleAllocator(n_pages, cap)
+    for op in ops:
+        if op[0] == "alloc":
+            _, sid, count, got, err = op
+            mine, e = [], ""
+            for _ in range(count):
+                try:
+                    mine.append(oa.allocate_page(sid))
+                except RuntimeError as x:
+                    e = str(x)
+                    break
+            if tuple(mine) != got or e != err:
+                return False
+        elif op[0] == "touch":
+            oa.touch(sid=op[1])
+        else:
+            oa._release(op[1])
+    return oa.free == final_free
+
+
+def paged_stress_leg(device, rank=0, world=1, sync=None, verify=True):
+    """Config 5 on this GPU: its share of the 512 sessions (i % world == rank)
+    in a page pool of ~150 GB of fp16 K/V (36 layers x 2 heads x 128, 16-token
+    pages; capped by the free memory), simulated arrivals, 64 decode steps per
+    session (push + whole-session gather), LRU eviction under pressure."""
+    from infercache_b200.paged_cache import PAGE_SIZE, MultiSessionCache, PagePool, PagedCacheConfig
+    w = C5_WORKLOAD
+    L, H, D = w["layers"], w["heads"], w["d"]
+    tok_bytes = 2 * L * H * D * 2
+    free, _ = torch.cuda.mem_get_info(device)
+    src_tokens = w["max_len"] + 16
+    pool_bytes = min(w["pool_gb"] * 1e9, free - 12e9 - 2 * src_tokens * tok_bytes / 2)
+    n_pages = int(pool_bytes // (PAGE_SIZE * tok_bytes))
+    cap = -(-(w["max_len"] + w["decode_steps"]) // PAGE_SIZE) + 1
+    cfg = PagedCacheConfig(n_pages=n_pages, n_layers=L, n_heads=H, head_dim=D, dtype=torch.float16,
+                           device=str(device), max_pages_per_session=cap)
+    pool = PagePool(cfg)
+    g = torch.Generator(device=device).manual_seed(w["seed"])
+    src_k = torch.randn(L, H, src_tokens, D, generator=g, device=device, dtype=torch.float16)
+    src_v = torch.randn(L, H, src_tokens, D, generator=g, device=device, dtype=torch.float16)
+    ticks = iter(range(1, 1 << 62))
+    msc = MultiSessionCache(pool, clock=lambda: float(next(ticks)))
+    rec = _RecordingAllocator(msc.allocator)
+    msc.allocator = rec
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def tick_timer(fn):
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    trace = c5_trace(world, rank)
+    if sync is not None:
+        sync(None)
+    r = paged_stress(msc, trace, w["decode_steps"], src_k, src_v, tick_timer)
+    torch.cuda.synchronize()
+    ms = r["busy_ms"]
+    if sync is not None:
+        ms = sync(ms)
+    tokens = r["decode_tokens"] * world  # every rank serves its share; the slowest sets the time
+    out = {"workload": f"paged allocator stress: 512 sessions of U[256, 32768] tokens (seed 4), Poisson arrivals "
+                       f"(mean 5 ms), 64 decode steps each (push + whole-session gather), fp16 K/V 36 layers x 2 "
+                       f"heads x 128, 16-token pages, LRU eviction; sessions i % {world} on each of {world} GPUs",
+           "n_gpus": world, "pool_pages_per_gpu": n_pages, "pool_gb_per_gpu": n_pages * PAGE_SIZE * tok_bytes / 1e9,
+           "decode_tokens_per_s": tokens / (ms / 1e3), "unit": "session-tokens/s",
+           "gather_gb_per_s": r["gathered_bytes"] * world / (ms / 1e3) / 1e9,
+           "gather_note": "bytes read + written by the whole-session gathers / device time of the ticks (pushes "
+                          "and host scheduling included)",
+           **{k: r[k] for k in ("sim_ms", "busy_ms", "decode_tokens", "prompt_tokens", "dropped_by_lru",
+                                "lru_evictions", "peak_active", "fragmentation_mean", "fragmentation_max",
+                                "fragmentation_samples")}}
+    if verify and rank == 0:
+        out["allocator_trace_ops"] = len(rec.ops)
+        out["allocator_matches_oracle"] = replay_on_oracle(rec.ops, n_pages, cap, rec.inner.free_list())
+    del pool, src_k, src_v, msc
+    torch.cuda.empty_cache()
+    return out
+
+
 MODEL_WORKLOAD = dict(layers=36, hidden=2048, hq=16, hkv=2, d=128, intermediate=11008, vocab=151936,
                       sessions=16, prompt=2048, steps=512, seed=1)
 
@@ -675,7 +894,7 @@ def main():
                          "the spread)")
     ap.add_argument("--no-summary", action="store_true",
                     help="skip the secondary legs (summary scorer, paged gather, 7B-shaped decode, graph cache)")
-    ap.add_argument("--workload", choices=["decode", "summary", "graph", "model"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "summary", "graph", "model", "paged"], default="decode",
                     help="summary / graph: time only the summary-pass scorer / the graph cache (for profiling)")
     ap.add_argument("--summary-batch", type=int, default=0, help="sequences in the summary workload")
     args = ap.parse_args()
@@ -693,6 +912,25 @@ def main():
     if args.workload == "summary":
         if rank == 0:
             print(json.dumps(summary_leg(device, iters=args.steps, batch=args.summary_batch or None)), flush=True)
+        return
+    if args.workload == "paged":
+        if world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+            def sync(x):
+                if x is None:
+                    dist.barrier(device_ids=[local_rank])
+                    return None
+                t = torch.tensor([x], dtype=torch.float64, device=device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                return float(t.item())
+            res = paged_stress_leg(device, rank, world, sync)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            dist.destroy_process_group()
+        else:
+            print(json.dumps(paged_stress_leg(device)), flush=True)
         return
     if args.workload == "model":
         if rank == 0:

@@ -100,8 +100,11 @@ class PagePool:
                    layer_begin: int = 0) -> None:
         """Write k, v [L', H, T, D] as tokens start_token .. start_token+T-1 of
         the session whose pages are `page_ids`, layers layer_begin .. +L'."""
-        k = k.to(self.device, self.cfg.dtype).contiguous()
-        v = v.to(self.device, self.cfg.dtype).contiguous()
+        k = k.to(self.device, self.cfg.dtype)
+        v = v.to(self.device, self.cfg.dtype)
+        # strided sources go to the kernel as they are (rows must be contiguous)
+        if k.stride(-1) != 1 or k.stride() != v.stride():
+            k, v = k.contiguous(), v.contiguous()
         pid = self._page_ids(page_ids)
         a = _lib.ic_page_rows_args(pool=self._c_pool, page_ids=pid.data_ptr(), n_page_ids=len(page_ids),
                                    layer_begin=layer_begin, layer_end=layer_begin + k.shape[0],

@@ -173,3 +173,41 @@ def test_top_importance_tokens_order_matches_oracle():
     for k in (0, 3, 8, 20):
         idx, vals = view.top_importance_tokens(k)
         assert idx == [i for _, i in pairs[:k]] and vals == [x for x, _ in pairs[:k]]
+
+
+class _GatherPool(RecordingPool):
+    """RecordingPool whose gathers return shape-only tensors."""
+
+    def gather_rows(self, page_ids, n_tokens, layer_begin, layer_end):
+        c = self.cfg
+        K = torch.empty(layer_end - layer_begin, c.n_heads, n_tokens, c.head_dim, device="meta")
+        return K, K
+
+
+def test_paged_stress_host_logic_matches_oracle_allocator():
+    """The config-5 driver (bench.paged_stress) on the host with a recording
+    pool: Poisson-like arrivals into a pool far smaller than the sessions
+    need, so the allocator evicts least-recently-used sessions; every
+    allocation, error and the final free list agree with the oracle's
+    allocator replaying the recorded trace, evicted sessions are dropped, and
+    every surviving session decodes its 8 steps."""
+    import random
+    import bench
+    cfg = PagedCacheConfig(n_pages=60, n_layers=2, n_heads=2, head_dim=8, dtype=torch.float32, device="cpu",
+                           max_pages_per_session=30)
+    ticks = iter(range(1, 10 ** 9))
+    msc = MultiSessionCache(_GatherPool(cfg), clock=lambda: float(next(ticks)))
+    rec = bench._RecordingAllocator(msc.allocator)
+    msc.allocator = rec
+    rng = random.Random(4)
+    t, trace = 0.0, []
+    for i in range(40):
+        t += rng.expovariate(1 / 5.0)
+        trace.append((i, rng.randint(10, 300), t))
+    src = torch.zeros(2, 2, 400, 8)
+    r = bench.paged_stress(msc, trace, 8, src, src, tick_timer=lambda fn: (fn(), 4.0)[1])
+    assert r["lru_evictions"] > 0 and r["dropped_by_lru"] > 0
+    assert r["decode_tokens"] >= 8 * (40 - r["dropped_by_lru"] - 5)
+    assert 0.0 <= r["fragmentation_mean"] <= r["fragmentation_max"] < 1.0
+    assert bench.replay_on_oracle(rec.ops, 60, 30, rec.inner.free_list())
+    assert msc.allocator.free_pages() == 60  # every session departed or was dropped
