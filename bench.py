@@ -577,7 +577,7 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
                     continue
                 K, V = view.gather_all()
                 counts["decode"] += 1
-                counts["gathered"] += K.numel() * K.element_size() * 2
+                counts["gathered"] += 2 * 2 * K.numel() * K.element_size()  # K and V, read and written
                 active[sid][1] -= 1
             prune()
 

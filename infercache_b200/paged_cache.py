@@ -93,7 +93,10 @@ class PagePool:
     def _abs(self, page_id: int, slot: int) -> int:
         return page_id * PAGE_SIZE + slot
 
-    def _page_ids(self, page_ids: List[int]) -> torch.Tensor:
+    def _page_ids(self, page_ids) -> torch.Tensor:
+        """int32 page ids on the pool's device (a device tensor passes through)."""
+        if isinstance(page_ids, torch.Tensor):
+            return page_ids
         return torch.tensor(page_ids, dtype=torch.int32).to(self.device, non_blocking=True)
 
     def write_rows(self, page_ids: List[int], start_token: int, k: torch.Tensor, v: torch.Tensor,
@@ -137,7 +140,7 @@ class PagePool:
 
     def gather_session(self, layer: int, page_ids: List[int], n_tokens: int) -> Tuple[torch.Tensor, torch.Tensor]:
         """K, V [n_heads, n_tokens, head_dim] (paged_cache.py:172-200)."""
-        if not page_ids:
+        if len(page_ids) == 0:
             empty = torch.zeros(self.cfg.n_heads, 0, self.cfg.head_dim, dtype=self.cfg.dtype, device=self.device)
             return empty, empty
         n_tokens = min(n_tokens, len(page_ids) * PAGE_SIZE)
@@ -315,10 +318,32 @@ class PagedSessionView:
         self._pos = np.zeros(0, dtype=np.int64)
         self._imp = np.zeros(0, dtype=np.float64)
         self._lock = threading.Lock()
+        # the page list mirrored on the pool's device, uploaded as it grows, so
+        # writes and gathers pass a device pointer instead of re-sending the list
+        self._dev_pages: Optional[torch.Tensor] = None
+        self._dev_n = 0
 
     @property
     def n_tokens(self) -> int:
         return self._n_tokens
+
+    def _device_pages(self):
+        """The page list on the pool's device (its first len(self._pages) entries)."""
+        n = len(self._pages)
+        dev = getattr(self._pool, "device", None)
+        if dev is None or not isinstance(dev, torch.device) or dev.type != "cuda":
+            return self._pages
+        if self._dev_pages is None or self._dev_pages.numel() < n:
+            cap = max(64, 2 * n)
+            grown = torch.empty(cap, dtype=torch.int32, device=dev)
+            if self._dev_pages is not None and self._dev_n:
+                grown[:self._dev_n].copy_(self._dev_pages[:self._dev_n])
+            self._dev_pages = grown
+        if self._dev_n < n:
+            self._dev_pages[self._dev_n:n].copy_(torch.tensor(self._pages[self._dev_n:n], dtype=torch.int32),
+                                                 non_blocking=True)
+            self._dev_n = n
+        return self._dev_pages[:n]
 
     def _grow(self, n: int) -> None:
         if n > self._pos.shape[0]:
@@ -348,7 +373,7 @@ class PagedSessionView:
             self._pages.extend(got)
             fit = min(n_new, len(self._pages) * PAGE_SIZE - start)
             if fit > 0:
-                self._pool.write_rows(self._pages, start, k_states[:, :, :fit], v_states[:, :, :fit])
+                self._pool.write_rows(self._device_pages(), start, k_states[:, :, :fit], v_states[:, :, :fit])
                 self._grow(start + fit)
                 idx = np.arange(fit)
                 given = np.asarray(positions[:fit], dtype=np.int64)
@@ -364,12 +389,12 @@ class PagedSessionView:
             self._alloc.touch(self.session_id)
 
     def gather(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        return self._pool.gather_session(layer, self._pages, self._n_tokens)
+        return self._pool.gather_session(layer, self._device_pages(), self._n_tokens)
 
     def gather_all(self) -> Tuple[torch.Tensor, torch.Tensor]:
         """K, V [n_layers, n_heads, n_tokens, head_dim] in one launch."""
         n = min(self._n_tokens, len(self._pages) * PAGE_SIZE)
-        return self._pool.gather_rows(self._pages, n, 0, self._pool.cfg.n_layers)
+        return self._pool.gather_rows(self._device_pages(), n, 0, self._pool.cfg.n_layers)
 
     def to_hf_past_key_values(self, device: str = None):
         K, V = self.gather_all()
@@ -393,6 +418,7 @@ class PagedSessionView:
         with self._lock:
             self._alloc.release_session(self.session_id)
             self._pages, self._n_tokens = [], 0
+            self._dev_n = 0
             self._pos = np.zeros(0, dtype=np.int64)
             self._imp = np.zeros(0, dtype=np.float64)
 
