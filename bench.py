@@ -1132,7 +1132,7 @@ def main():
     h2d, d2h = stepper.h2d_bytes, stepper.d2h_bytes
     b.check_device_status()
 
-    summ = paged = c3 = graph = model = None
+    summ = paged = c3 = graph = model = paged_stress = None
     c3_strong = None
     if world > 1 and not args.no_summary and C3_WORKLOAD["sessions"] % world == 0:
         # config 3 split across the ranks: the 64 sessions, max time over ranks
@@ -1153,6 +1153,8 @@ def main():
         c3 = config3_leg(device)
         log("model leg")
         model = model_leg(device)
+        log("paged allocator stress leg")
+        paged_stress = paged_stress_leg(device)
         log("graph cache leg")
         graph = graph_leg(device, cpu_sample=256 if (rank == 0 and world == 1 and not args.no_cpu_baseline) else 0)
 
@@ -1205,7 +1207,8 @@ def main():
                 "decode_7b_shape": c3,
                 "decode_7b_shape_strong": c3_strong,
                 "graph_cache": graph,
-                "model_decode_3b": model}
+                "model_decode_3b": model,
+                "paged_stress": paged_stress}
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphs
