@@ -1047,8 +1047,13 @@ def main():
         return max_over_ranks(e0.elapsed_time(e1))
 
     ms = timed_steps()  # the measurement the line reports
-    # the same K steps again, for the spread between runs (not part of `value`)
-    repeats = [ms] + [timed_steps() for _ in range(max(0, args.repeats - 1))]
+    # the same K steps again, for the spread between runs (not part of `value`):
+    # at least --repeats runs and at least ~0.5 s of them, so a short K still
+    # gives a spread and clock samples under load
+    n_rep = max(args.repeats, min(400, int(500.0 / max(ms, 1e-3)) + 1))
+    if world > 1:
+        n_rep = int(max_over_ranks(n_rep))
+    repeats = [ms] + [timed_steps() for _ in range(max(0, n_rep - 1))]
     if sampler:
         sampler.stop()
     value = world * S * args.steps / (ms / 1e3)
@@ -1190,9 +1195,10 @@ def main():
                              "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
                 "cpu_baseline": cpu,
                 "cpu_baselines_other": cpu_other,
-                "repeats": {"ms_per_step": [r / args.steps for r in repeats],
+                "repeats": {"ms_per_step": [r / args.steps for r in repeats[:20]],
                             "median_ms_per_step": statistics.median(repeats) / args.steps,
                             "spread": (max(repeats) - min(repeats)) / statistics.median(repeats),
+                            "runs": len(repeats),
                             "note": "the same K steps run back to back; value is the first"},
                 "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "steps": ke, "api": e2e_api},
