@@ -5,7 +5,8 @@
 // The launch fills the machine on its own: the budget + 1 logical slots of a
 // (session, KV head) group are cut into CL chunks of 16-slot blocks, one CTA
 // per chunk, the group's CTAs one thread-block cluster.  At 16 sessions x 2 KV
-// heads x 1041 slots with CL = 8: 256 CTAs of five warps, 144 slots each.
+// heads x 1041 slots with CL = 8: 256 CTAs of nine warps, 144 slots each (one
+// 16-slot block per warp; two per warp only when a chunk has more than nine).
 // Per CTA:
 //   1. every warp looks up its one or two 16-slot blocks in the session's slot
 //      table and copies their K rows, then their V rows, into padded shared-
@@ -42,7 +43,7 @@ namespace ic {
 namespace {
 
 constexpr int SP_D = 128;
-constexpr int SP_MAXW = 8;                  // warps per CTA at most
+constexpr int SP_MAXW = 9;                  // warps per CTA at most
 constexpr int SP_MAXCL = 16;                // CTAs per cluster at most
 constexpr int SP_PITCH = SP_D * 2 + 16;     // padded row: conflict-free ldmatrix
 constexpr float SP_LOG2E = 1.4426950408889634f;
