@@ -356,6 +356,39 @@ class SessionBatch:
         _lib.call("ic_evict_update", e)
         self._keep = (k, v, mass, pos)
 
+    def append(self, k: torch.Tensor, v: torch.Tensor, positions) -> None:
+        """The new token of every session appended at once, without attention:
+        k / v [L, S, Hkv, D] (any float dtype, on any device), positions [S].
+        One staging-row write over all sessions and layers, then kernel B with
+        no importance boost and no decay -- for every session what the
+        reference's ``push(key, value, position)`` without ``attn_weights``
+        does (hierarchical_cache.py:241-294), e.g. the two-pass loop's push
+        (two_pass.py:326-336)."""
+        cfg = self.cfg
+        S = self.num_sessions
+        want = (cfg.num_layers, S, cfg.num_kv_heads, cfg.head_dim)
+        if tuple(k.shape) != want or k.shape != v.shape:
+            raise ValueError(f"k / v must be [L, S, Hkv, D] = {list(want)}")
+        k = k.to(self.device, cfg.dtype)
+        v = v.to(self.device, cfg.dtype)
+        if k.stride(-1) != 1 or k.stride() != v.stride():
+            k, v = k.contiguous(), v.contiguous()
+        a = _lib.ic_append_args(pool=self._c_pool, tiers=self._c_tiers, sess=self._c_sess, k=k.data_ptr(),
+                                v=v.data_ptr(), stride_s=k.stride(1), stride_l=k.stride(0), stride_h=k.stride(2))
+        _lib.call("ic_append_staging", a)
+        pos = self._positions_arg(positions)
+        e = self._ev
+        e.new_pos = pos.data_ptr()
+        e.decay = 1.0
+        e.mass = 0
+        e.mass_heads = cfg.num_kv_heads
+        e.mass_layers = 1
+        e.mass_div = 1.0
+        e.pdl = 0
+        e.advance_pos = 0
+        _lib.call("ic_evict_update", e)
+        self._keep = (k, v, pos)
+
     # ---- priming, export, reset ------------------------------------------------------------
     def load_prompt(self, session: int, past_key_values, importance_scores: torch.Tensor,
                     positions: Optional[torch.Tensor] = None) -> None:

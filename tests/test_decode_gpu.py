@@ -729,3 +729,36 @@ def test_device_timeout_is_reported_and_context_survives():
     torch.cuda.synchronize()
     assert torch.isfinite(o.float()).all()
     b.check_device_status()
+
+
+def test_batched_append_matches_per_session_push():
+    """SessionBatch.append (every session's token in one launch, kernel B
+    without a boost) leaves exactly the state of the reference-compatible
+    push(key, value, position) without weights called session by session,
+    over enough steps that ring tokens are dropped for a zero score."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    cfg = CacheConfig(num_layers=3, num_kv_heads=2, head_dim=128, sink_size=2, recent_size=6, important_size=5,
+                      dtype=torch.float16)
+    S, L = 4, 3
+    g = torch.Generator().manual_seed(21)
+    pk = torch.randn(L, 2, 30, 128, generator=g).half()
+    sc = torch.rand(30, generator=g)
+    batches = [SessionBatch(cfg, S, "cuda:0") for _ in range(2)]
+    for b in batches:
+        for s in range(S):
+            b.load_prompt(s, tuple((pk[l][None], pk[l][None]) for l in range(L)), sc)
+    for t in range(12):
+        k = torch.randn(L, S, 2, 128, generator=g).half()
+        v = torch.randn(L, S, 2, 128, generator=g).half()
+        batches[0].append(k.cuda(), v.cuda(), [30 + t] * S)
+        for s in range(S):
+            batches[1].push(s, k[:, s, :, None, :], v[:, s, :, None, :], 30 + t)
+        assert torch.equal(batches[0].events, batches[1].events), t
+    a, b = batches
+    for name in ("slot_table", "positions", "importance", "occupied", "ctrl", "counters"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name
+    for s in range(S):
+        Ka, Va = a.gather(s)
+        Kb, Vb = b.gather(s)
+        assert torch.equal(Ka, Kb) and torch.equal(Va, Vb)
+    a.check_device_status()
