@@ -762,3 +762,12 @@ def test_batched_append_matches_per_session_push():
         Kb, Vb = b.gather(s)
         assert torch.equal(Ka, Kb) and torch.equal(Va, Vb)
     a.check_device_status()
+
+
+@pytest.mark.parametrize("variant", [0, 5])
+def test_attend_split_kernel_partly_filled(variant):
+    """The slot-split kernel on a cache whose prompt (5 tokens) is shorter than
+    its budget: empty slots in every tier while it fills, against the oracle."""
+    sp = dict(specs.SMALL["short_prompt"])
+    cache, oc, outs, events = run_small_attend(sp, "float16", variant)
+    cache.batch.check_device_status()
