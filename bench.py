@@ -1183,6 +1183,7 @@ def main():
                 "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": config_dict(spec, world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": traffic,
+                             "frac_of_nominal_8tbs": achieved / 8000.0,
                              "kernel": "decode_lean_kernel (ic_decode_step); unit = one layer of all 16 sessions "
                                        f"({groups} launches of {S // groups} sessions when grouped)",
                              "alg_bytes_per_launch": alg_bytes, "launch_us": dec_launch_s * 1e6,
@@ -1192,6 +1193,8 @@ def main():
                                                          "shared memory (attend, one layer at a time)",
                              "sequential_attend_us": seq_launch_s * 1e6,
                              "sequential_attend_frac": alg_bytes / seq_launch_s / 1e9 / peak,
+                             "traffic_basis": "dram__bytes_read + dram__bytes_write of one decode_lean_kernel launch "
+                                              "of 16 sessions (profiles/decode_layer_c2.md)",
                              "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
                 "cpu_baseline": cpu,
                 "cpu_baselines_other": cpu_other,
