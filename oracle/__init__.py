@@ -2,8 +2,9 @@
 
 TEST INFRASTRUCTURE ONLY.  Nothing in ``infercache_b200`` imports this
 package: only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline
-legs of ``bench.py`` use it, and only as the checker or as the timed CPU
-baseline, never as a product code path.
+legs of ``bench.py`` use it, and only to check results or as the timed CPU
+baseline, never as a product code path.  ``ref_fleet`` and ``ref_install``
+run and install the reference itself for that baseline.
 
 The oracle is a numpy restatement of the reference implementation
 (the ``inference`` package of ravirajb/infercache):
