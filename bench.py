@@ -519,7 +519,9 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
     (PagedSessionView.push of their prompt), then decode `decode_steps` tokens
     -- per step one token pushed and the session's whole page list gathered
     into HF layout (to_hf_past_key_values, paged_cache.py:365-378) -- and
-    depart (reset).  A tick serves every active session once; its duration is
+    depart (reset).  A tick serves every active session once, the pushes and
+    gathers of its sessions batched (MultiSessionCache.push_many /
+    gather_many, up to 32 sessions and 2 GiB of output per gather launch); its duration is
     `tick_timer(fn)` (device time around fn) and advances the clock.  When the
     pool runs out, the allocator evicts the least recently used session; a
     session that lost its pages that way is dropped.  Returns counters and the
@@ -536,6 +538,9 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
     peak_active = 0
     alloc = msc.allocator
     tok_k, tok_v = src_k[:, :, :1], src_v[:, :, :1]
+    from infercache_b200 import _lib
+    row_bytes = src_k.shape[0] * src_k.shape[1] * src_k.shape[3] * src_k.element_size()  # one token, all layers
+    gather_budget = 2 << 30  # output bytes of one batched gather launch
 
     def admit(sid, n):
         nonlocal prompt_tokens
@@ -549,7 +554,7 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
 
     def prune():
         nonlocal dropped
-        for sid in [k for k, a in active.items() if not alloc.pages_for(str(k))]:
+        for sid in [k for k, a in active.items() if not alloc.page_count(str(k))]:
             msc.reset(str(sid))
             del active[sid]
             dropped += 1
@@ -567,18 +572,28 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
             for sid, n, _ in arrivals:
                 admit(sid, n)
             prune()
-            for sid in list(active):
-                view = active[sid][0]
-                try:
-                    view.push(tok_k, tok_v, positions=[], importance=[])
-                except RuntimeError:
-                    pass  # at the cap the session decodes over what it holds
-                if not alloc.pages_for(str(sid)):
-                    continue
-                K, V = view.gather_all()
-                counts["decode"] += 1
-                counts["gathered"] += 2 * 2 * K.numel() * K.element_size()  # K and V, read and written
-                active[sid][1] -= 1
+            sids = list(active)
+            # the sessions in chunks of up to 32: one token each (errors at the
+            # per-session cap are ignored: such a session decodes over what it
+            # holds), written in one launch with the allocator calls of a
+            # per-session loop, then the chunk's whole-session gathers in one
+            # launch (or more, at most gather_budget bytes of output each), so
+            # the next chunk's host work overlaps this chunk's copies
+            step = _lib.IC_PAGE_BATCH_MAX
+            for c0 in range(0, len(sids), step):
+                chunk = sids[c0:c0 + step]
+                msc.push_many([str(x) for x in chunk], [tok_k] * len(chunk), [tok_v] * len(chunk))
+                live = [x for x in chunk if alloc.page_count(str(x))]
+                group, size = [], 0
+                for i, x in enumerate(live):
+                    group.append(x)
+                    size += 2 * active[x][0].n_tokens * row_bytes
+                    if size >= gather_budget or i == len(live) - 1:
+                        for y, (K, V) in zip(group, msc.gather_many([str(z) for z in group])):
+                            counts["decode"] += 1
+                            counts["gathered"] += 2 * 2 * K.numel() * K.element_size()  # K and V, read and written
+                            active[y][1] -= 1
+                        group, size = [], 0
             prune()
 
         dt = tick_timer(tick)

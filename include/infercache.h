@@ -190,7 +190,10 @@ typedef struct ic_evict_args {
   int32_t mass_layers;
   float mass_div;
   float decay;
-  int32_t pdl;             /* 1: launch with programmatic dependent launch */
+  int32_t pdl;             /* 1: launch with programmatic dependent launch; 2: the
+                              same, and the kernel before it on the stream writes
+                              none of the session state but the mass (a kernel-A
+                              layer): that state is staged before the wait */
   int32_t advance_pos;     /* 1: new_pos[s] += 1 once read (the next step's position) */
   int64_t* new_pos;        /* [S] */
   int64_t* events;         /* [S, 4] record of this step, or NULL */
@@ -350,6 +353,18 @@ typedef struct ic_page_rows_args {
 } ic_page_rows_args;
 int ic_page_gather(const ic_page_rows_args* a, void* stream);
 int ic_page_write(const ic_page_rows_args* a, void* stream);
+
+/* The same for `count` page lists (1 <= count <= IC_PAGE_BATCH_MAX) in one
+ * launch: a[i] is one session's gather or write as above.  Every descriptor
+ * names the same pool and layer range; each has its own page list, token
+ * range and buffers.  Replaces a host loop of gather_session /
+ * to_hf_past_key_values (paged_cache.py:172-200, 365-378) or of one-token
+ * pushes (:330-363) over the sessions served in one decode tick.  Writes of
+ * two descriptors to the same pool row race (the caller keeps page lists
+ * disjoint, as the allocator does). */
+#define IC_PAGE_BATCH_MAX 32
+int ic_page_gather_batch(const ic_page_rows_args* a, int32_t count, void* stream);
+int ic_page_write_batch(const ic_page_rows_args* a, int32_t count, void* stream);
 
 /* ---- Kernel C: summary-pass scorer (tcgen05 / TMEM) -----------------------
  * Causal GQA attention over a prompt, P = softmax(scale * Q K^T) with query

@@ -212,6 +212,12 @@ ENTRY_POINTS = {
     "ic_graph_push": ic_graph_push_args,
     "ic_graph_select": ic_graph_select_args,
 }
+# entry points over an array of argument structs: (const args*, int32 count, stream)
+BATCH_ENTRY_POINTS = {
+    "ic_page_gather_batch": ic_page_rows_args,
+    "ic_page_write_batch": ic_page_rows_args,
+}
+IC_PAGE_BATCH_MAX = 32
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
 HOST_ENTRY_POINTS = ["ic_host_device_pointer", "ic_wait_probe"]
 
@@ -230,6 +236,10 @@ def load(path: Path = LIB_PATH):
     for name, st in ENTRY_POINTS.items():
         fn = getattr(lib, name)
         fn.argtypes = [POINTER(st), c_void_p]
+        fn.restype = c_int
+    for name, st in BATCH_ENTRY_POINTS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = [POINTER(st), c_int32, c_void_p]
         fn.restype = c_int
     lib.ic_status_str.argtypes = [c_int]
     lib.ic_status_str.restype = c_char_p
@@ -264,6 +274,16 @@ def call(name: str, args) -> None:
     lib = load()
     stream = torch.cuda.current_stream().cuda_stream
     raise_for(getattr(lib, name)(ctypes.byref(args), c_void_p(stream)), name)
+
+
+def call_batch(name: str, args) -> None:
+    """Call batch entry point `name` with a list of structs (at most
+    IC_PAGE_BATCH_MAX) on torch's current CUDA stream."""
+    lib = load()
+    stream = torch.cuda.current_stream().cuda_stream
+    st = BATCH_ENTRY_POINTS[name]
+    arr = (st * len(args))(*args)
+    raise_for(getattr(lib, name)(arr, len(args), c_void_p(stream)), name)
 
 
 _DEVICE_OK = {}

@@ -407,5 +407,9 @@ extern "C" int ic_decode_step(const ic_step_args* a, void* stream) {
     const int rc = ic_decode_layer(&d, stream);
     if (rc != IC_OK) return rc;
   }
-  return ic_evict_update(&a->evict, stream);
+  // the eviction follows a kernel-A layer, which writes none of the session
+  // state it stages: that staging need not wait for the layer
+  ic_evict_args e = a->evict;
+  if (e.pdl == 1) e.pdl = 2;
+  return ic_evict_update(&e, stream);
 }

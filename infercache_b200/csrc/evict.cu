@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(IU_THREADS) importance_update_kernel(const ic_
 
 template <bool REDUCED>
 __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a) {
-  // shared: importance [budget], positions [budget], slot table [budget + 1]
+  // shared: positions [budget], importance [budget], slot table [budget + 1],
+  // occupancy [budget]
   extern __shared__ __align__(16) unsigned char ev_smem[];
   __shared__ float red_v[EV_THREADS / 32];
   __shared__ int red_i[EV_THREADS / 32];
@@ -111,23 +112,26 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   int64_t* pos = a.sess.positions + static_cast<size_t>(s) * B;
   int32_t* stt = a.sess.slot_table + static_cast<size_t>(s) * ntot;
 
-  // launched with programmatic dependent launch: the last layer's mass must
-  // be complete before it is read; the next step's first layer waits for us
-  grid_dependency_wait();
-  grid_launch_dependents();
+  uint8_t* occ_s = reinterpret_cast<uint8_t*>(stt_s + ntot);
 
-  // 1. decay + boost of every occupied slot (already applied when REDUCED);
-  // the slot table and positions are staged too, so the decision below reads
-  // shared memory only
+  // Launched with programmatic dependent launch: the mass must be complete
+  // before it is read, and the next step's first layer waits for us.  With
+  // pdl == 2 the kernel before this one writes none of the session state read
+  // here (kernel A writes only the mass, `out` and the staging rows), so that
+  // state is staged first and only the mass waits.
+  const bool stage_early = !REDUCED && a.pdl == 2;
+  if (!stage_early) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+  }
+
+  // 1. stage the slot table, positions, importance and occupancy, so the
+  // decision below reads shared memory only
   for (int j = tid; j < ntot; j += EV_THREADS) stt_s[j] = stt[j];
   for (int j = tid; j < B; j += EV_THREADS) {
     pos_s[j] = pos[j];
-    float v = imp[j];
-    if (!REDUCED && occ[j]) {
-      v = updated_importance(a, s, j, v);
-      imp[j] = v;
-    }
-    imp_s[j] = v;
+    imp_s[j] = imp[j];
+    occ_s[j] = occ[j];
   }
   // Snapshot the decision inputs: every thread must branch identically, and
   // thread 0 rewrites ctrl / occupied below.
@@ -138,7 +142,6 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
     snap_fill = ctrl[IC_CTRL_IMPORTANT_FILL];
     snap_rf = ctrl[IC_CTRL_RECENT_FILL];
     snap_newpos = a.new_pos[s];
-    if (a.advance_pos) a.new_pos[s] = snap_newpos + 1;  // the next step's position
     for (int i = 0; i < IC_COUNTER_WORDS; ++i) snap_cnt[i] = cnt[i];
     const bool ok = snap_r >= sink && snap_r < l2s && snap_fill >= 0 && snap_fill <= cap;
     if (!ok) {
@@ -148,6 +151,21 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
       snap_disp = occ[snap_r] != 0;
     }
   }
+  if (stage_early) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+  }
+  // decay + boost of every occupied slot (already applied when REDUCED); each
+  // thread updates the slots it staged
+  if (!REDUCED) {
+    for (int j = tid; j < B; j += EV_THREADS) {
+      if (!occ_s[j]) continue;
+      const float v = updated_importance(a, s, j, imp_s[j]);
+      imp[j] = v;
+      imp_s[j] = v;
+    }
+  }
+  if (tid == 0 && a.advance_pos) a.new_pos[s] = snap_newpos + 1;  // the next step's position
   __syncthreads();
   if (snap_r < 0) return;  // corrupted ring state: reported, nothing written
 
@@ -374,11 +392,12 @@ extern "C" int ic_evict_update(const ic_evict_args* a, void* stream) {
   if (a->sess.num_sessions == 0) return IC_OK;
   if (!tiers_ok(a->tiers) || a->sess.num_sessions < 0 || !a->new_pos || !a->sess.slot_table ||
       !a->sess.positions || !a->sess.importance || !a->sess.occupied || !a->sess.ctrl ||
-      !a->sess.counters || (a->mass && (a->mass_heads < 1 || a->mass_layers < 1 || !(a->mass_div > 0.f)))) {
+      !a->sess.counters || (a->mass && (a->mass_heads < 1 || a->mass_layers < 1 || !(a->mass_div > 0.f))) ||
+      a->pdl < 0 || a->pdl > 2) {
     set_last_error("evict_update: bad arguments");
     return IC_ERR_INVALID_ARG;
   }
-  const size_t smem = static_cast<size_t>(a->tiers.budget) * (sizeof(int64_t) + sizeof(float)) +
+  const size_t smem = static_cast<size_t>(a->tiers.budget) * (sizeof(int64_t) + sizeof(float) + 1) +
                      static_cast<size_t>(a->tiers.budget + 1) * sizeof(int32_t);
   if (smem > 200 * 1024) { set_last_error("evict_update: budget too large"); return IC_ERR_UNSUPPORTED; }
   // With many mass columns to sum, the per-slot update runs as its own wide

@@ -80,6 +80,60 @@ __global__ void page_rows_kernel(const ic_page_rows_args a, int vecs) {
   }
 }
 
+// Many page lists in one launch: the descriptors travel as the kernel's
+// parameter block (read in place through __grid_constant__); block x of the
+// grid belongs to descriptor i when blk_off[i] <= x < blk_off[i + 1].
+struct PageDesc {
+  const int32_t* page_ids;
+  char* k_buf;
+  char* v_buf;
+  int64_t n_page_ids, start_token, n_tokens;
+  int64_t stride_l, stride_h, stride_t;
+};
+
+struct PageBatch {
+  ic_pool pool;
+  int32_t layer_begin, count;
+  int32_t blk_off[IC_PAGE_BATCH_MAX + 1];
+  PageDesc d[IC_PAGE_BATCH_MAX];
+};
+
+template <bool WRITE>
+__global__ void page_rows_batch_kernel(const __grid_constant__ PageBatch b, int vecs) {
+  const int bx = blockIdx.x;
+  int i = 0;
+  while (i + 1 < b.count && b.blk_off[i + 1] <= bx) ++i;
+  const PageDesc& d = b.d[i];
+  const int h = blockIdx.y;
+  const int lz = blockIdx.z;
+  const int l = b.layer_begin + lz;
+  const int H = b.pool.num_kv_heads;
+  const int esz = b.pool.dtype == IC_F32 ? 4 : 2;
+  const size_t row_bytes = static_cast<size_t>(b.pool.head_dim) * esz;
+  char* poolk = static_cast<char*>(b.pool.k) + (static_cast<size_t>(l) * H + h) * b.pool.pool_tokens * row_bytes;
+  char* poolv = static_cast<char*>(b.pool.v) + (static_cast<size_t>(l) * H + h) * b.pool.pool_tokens * row_bytes;
+  const int per_block = blockDim.x / vecs;
+  const int vi = threadIdx.x % vecs, ri = threadIdx.x / vecs;
+  if (ri >= per_block) return;
+  const int64_t t = static_cast<int64_t>(bx - b.blk_off[i]) * per_block + ri;
+  if (t >= d.n_tokens) return;
+  const int64_t lt = d.start_token + t;
+  if (lt >= d.n_page_ids * PAGE) return;
+  const int64_t row = page_row(d.page_ids, lt);
+  if (row < 0 || row >= b.pool.pool_tokens) return;
+  const int64_t bo = (lz * d.stride_l + h * d.stride_h + t * d.stride_t) * esz;
+  int4* pk = reinterpret_cast<int4*>(poolk + row * row_bytes) + vi;
+  int4* pv = reinterpret_cast<int4*>(poolv + row * row_bytes) + vi;
+  int4* bk = reinterpret_cast<int4*>(d.k_buf + bo) + vi;
+  int4* bv = reinterpret_cast<int4*>(d.v_buf + bo) + vi;
+  if (WRITE) { *pk = *bk; *pv = *bv; } else { *bk = *pk; *bv = *pv; }
+}
+
+static bool same_pool(const ic_pool& x, const ic_pool& y) {
+  return x.k == y.k && x.v == y.v && x.pool_tokens == y.pool_tokens && x.num_layers == y.num_layers &&
+         x.num_kv_heads == y.num_kv_heads && x.head_dim == y.head_dim && x.dtype == y.dtype;
+}
+
 static int row_vecs(const ic_pool& p) {
   const int esz = p.dtype == IC_F32 ? 4 : 2;
   const int bytes = p.head_dim * esz;
@@ -109,19 +163,25 @@ extern "C" int ic_gather_slots(const ic_gather_args* a, void* stream) {
   return launch_status("gather_slots");
 }
 
-static int page_rows(const ic_page_rows_args* a, void* stream, bool write) {
-  if (!a) return IC_ERR_INVALID_ARG;
-  if (a->n_tokens == 0 || a->layer_end == a->layer_begin) return IC_OK;
-  const int vecs = row_vecs(a->pool);
-  if (vecs < 0) { set_last_error("page rows: row size must be a multiple of 16 bytes"); return IC_ERR_UNSUPPORTED; }
+// Argument checks shared by the single and batched forms (a non-empty token
+// range and layer range).
+static bool page_rows_ok(const ic_page_rows_args* a) {
   const int esz = a->pool.dtype == IC_F32 ? 4 : 2;
   const bool aligned = ((a->stride_l * esz) % 16 == 0) && ((a->stride_h * esz) % 16 == 0) &&
                        ((a->stride_t * esz) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(a->k_buf) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(a->v_buf) % 16 == 0);
-  if (a->n_tokens < 0 || !a->page_ids || !a->k_buf || !a->v_buf || !a->pool.k || !a->pool.v || !aligned ||
-      a->layer_begin < 0 || a->layer_end > a->pool.num_layers || a->layer_begin > a->layer_end ||
-      a->start_token < 0 || a->start_token + a->n_tokens > static_cast<int64_t>(a->n_page_ids) * PAGE) {
+  return !(a->n_tokens < 0 || !a->page_ids || !a->k_buf || !a->v_buf || !a->pool.k || !a->pool.v || !aligned ||
+           a->layer_begin < 0 || a->layer_end > a->pool.num_layers || a->layer_begin > a->layer_end ||
+           a->start_token < 0 || a->start_token + a->n_tokens > static_cast<int64_t>(a->n_page_ids) * PAGE);
+}
+
+static int page_rows(const ic_page_rows_args* a, void* stream, bool write) {
+  if (!a) return IC_ERR_INVALID_ARG;
+  if (a->n_tokens == 0 || a->layer_end == a->layer_begin) return IC_OK;
+  const int vecs = row_vecs(a->pool);
+  if (vecs < 0) { set_last_error("page rows: row size must be a multiple of 16 bytes"); return IC_ERR_UNSUPPORTED; }
+  if (!page_rows_ok(a)) {
     set_last_error("page rows: bad arguments");
     return IC_ERR_INVALID_ARG;
   }
@@ -137,5 +197,56 @@ static int page_rows(const ic_page_rows_args* a, void* stream, bool write) {
   return launch_status(write ? "page_write" : "page_gather");
 }
 
+static int page_rows_batch(const ic_page_rows_args* a, int32_t count, void* stream, bool write) {
+  if (!a || count < 1 || count > IC_PAGE_BATCH_MAX) {
+    set_last_error("page rows (batch): 1 <= count <= IC_PAGE_BATCH_MAX descriptors");
+    return IC_ERR_INVALID_ARG;
+  }
+  const int vecs = row_vecs(a[0].pool);
+  if (vecs < 0) { set_last_error("page rows: row size must be a multiple of 16 bytes"); return IC_ERR_UNSUPPORTED; }
+  PageBatch b = {};
+  b.pool = a[0].pool;
+  b.layer_begin = a[0].layer_begin;
+  b.count = count;
+  const int per_block = 256 / vecs;
+  int64_t blocks = 0;
+  for (int i = 0; i < count; ++i) {
+    const ic_page_rows_args& x = a[i];
+    if (!same_pool(x.pool, a[0].pool) || x.layer_begin != a[0].layer_begin || x.layer_end != a[0].layer_end ||
+        (x.n_tokens != 0 && !page_rows_ok(&x)) || x.n_tokens < 0) {
+      set_last_error("page rows (batch): bad arguments, or descriptors on different pools or layer ranges");
+      return IC_ERR_INVALID_ARG;
+    }
+    b.blk_off[i] = static_cast<int32_t>(blocks);
+    b.d[i] = PageDesc{x.page_ids, static_cast<char*>(x.k_buf), static_cast<char*>(x.v_buf), x.n_page_ids,
+                      x.start_token, x.n_tokens, x.stride_l, x.stride_h, x.stride_t};
+    blocks += (x.n_tokens + per_block - 1) / per_block;
+    if (blocks > 0x7fffffff) {
+      set_last_error("page rows (batch): too many tokens for one launch");
+      return IC_ERR_UNSUPPORTED;
+    }
+  }
+  b.blk_off[count] = static_cast<int32_t>(blocks);
+  const int layers = a[0].layer_end - a[0].layer_begin;
+  if (blocks == 0 || layers == 0) return IC_OK;
+  if (a[0].layer_begin < 0 || a[0].layer_end > a[0].pool.num_layers || layers < 0) {
+    set_last_error("page rows (batch): bad layer range");
+    return IC_ERR_INVALID_ARG;
+  }
+  dim3 grid(static_cast<unsigned>(blocks), a[0].pool.num_kv_heads, layers);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (write)
+    page_rows_batch_kernel<true><<<grid, 256, 0, st>>>(b, vecs);
+  else
+    page_rows_batch_kernel<false><<<grid, 256, 0, st>>>(b, vecs);
+  return launch_status(write ? "page_write (batch)" : "page_gather (batch)");
+}
+
 extern "C" int ic_page_gather(const ic_page_rows_args* a, void* stream) { return page_rows(a, stream, false); }
 extern "C" int ic_page_write(const ic_page_rows_args* a, void* stream) { return page_rows(a, stream, true); }
+extern "C" int ic_page_gather_batch(const ic_page_rows_args* a, int32_t count, void* stream) {
+  return page_rows_batch(a, count, stream, false);
+}
+extern "C" int ic_page_write_batch(const ic_page_rows_args* a, int32_t count, void* stream) {
+  return page_rows_batch(a, count, stream, true);
+}

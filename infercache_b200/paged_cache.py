@@ -16,6 +16,7 @@ under a lock, paged_cache.py:205-288).
 """
 from __future__ import annotations
 
+import contextlib
 import heapq
 import threading
 import time
@@ -138,6 +139,50 @@ class PagePool:
         _lib.call("ic_page_gather", a)
         return K, V
 
+    def _rows_args(self, page_ids: torch.Tensor, n_page_ids: int, start: int, k: torch.Tensor, v: torch.Tensor,
+                   layer_begin: int) -> _lib.ic_page_rows_args:
+        return _lib.ic_page_rows_args(pool=self._c_pool, page_ids=page_ids.data_ptr(), n_page_ids=n_page_ids,
+                                      layer_begin=layer_begin, layer_end=layer_begin + k.shape[0],
+                                      start_token=start, n_tokens=k.shape[2], k_buf=k.data_ptr(),
+                                      v_buf=v.data_ptr(), stride_l=k.stride(0), stride_h=k.stride(1),
+                                      stride_t=k.stride(2))
+
+    def _run_batches(self, name: str, descs: List[_lib.ic_page_rows_args]) -> None:
+        step = _lib.IC_PAGE_BATCH_MAX
+        for i in range(0, len(descs), step):
+            _lib.call_batch(name, descs[i:i + step])
+
+    def write_rows_many(self, items) -> None:
+        """write_rows for several page lists, all layers from 0: items are
+        (page_ids, start_token, k, v) with k, v [L, H, T, D]; one launch per
+        IC_PAGE_BATCH_MAX items.  The page lists must not share pool rows."""
+        descs, keep = [], []
+        for page_ids, start, k, v in items:
+            if k.shape[2] == 0:
+                continue
+            k = k.to(self.device, self.cfg.dtype)
+            v = v.to(self.device, self.cfg.dtype)
+            if k.stride(-1) != 1 or k.stride() != v.stride():
+                k, v = k.contiguous(), v.contiguous()
+            pid = self._page_ids(page_ids)
+            keep.append((pid, k, v))
+            descs.append(self._rows_args(pid, len(page_ids), start, k, v, 0))
+        self._run_batches("ic_page_write_batch", descs)
+
+    def gather_rows_many(self, items) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+        """gather_rows(page_ids, n_tokens, 0, n_layers) for several page lists:
+        items are (page_ids, n_tokens); one launch per IC_PAGE_BATCH_MAX items."""
+        c = self.cfg
+        outs, descs = [], []
+        for page_ids, n in items:
+            K = torch.empty(c.n_layers, c.n_heads, n, c.head_dim, dtype=c.dtype, device=self.device)
+            V = torch.empty_like(K)
+            outs.append((K, V))
+            if n > 0:
+                descs.append(self._rows_args(self._page_ids(page_ids), len(page_ids), 0, K, V, 0))
+        self._run_batches("ic_page_gather_batch", descs)
+        return outs
+
     def gather_session(self, layer: int, page_ids: List[int], n_tokens: int) -> Tuple[torch.Tensor, torch.Tensor]:
         """K, V [n_heads, n_tokens, head_dim] (paged_cache.py:172-200)."""
         if len(page_ids) == 0:
@@ -179,6 +224,7 @@ class KVAllocator:
         self.max_pages_per_session = int(max_pages_per_session)
         self._stack = np.arange(self.n_pages, dtype=np.int32)
         self._top = self.n_pages
+        self._owner = np.full(self.n_pages, -1, dtype=np.int64)  # page -> creation rank of its lease
         self._leases: Dict[str, _Lease] = {}
         self._tokens: Dict[str, int] = {}
         self._lru: List[Tuple[float, int, str]] = []
@@ -199,6 +245,7 @@ class KVAllocator:
             n = len(lease.pages)
             self._stack[self._top:self._top + n] = lease.pages
             self._top += n
+            self._owner[lease.pages] = -1
 
     def _victim(self) -> str:
         while self._lru:
@@ -224,6 +271,7 @@ class KVAllocator:
         self._top -= 1
         page = int(self._stack[self._top])
         lease.pages.append(page)
+        self._owner[page] = lease.rank
         self._stamp(session_id, lease)
         if len(self._lru) > 4 * len(self._leases) + 64:  # drop stale heap entries now and then
             self._lru = [(lz.stamp, lz.rank, sid) for sid, lz in self._leases.items()]
@@ -249,6 +297,18 @@ class KVAllocator:
                 except RuntimeError as e:
                     return got, e
         return got, None
+
+    def page_count(self, session_id: str) -> int:
+        """How many pages `session_id` holds (len(pages_for(...)) without the copy)."""
+        with self._mu:
+            lease = self._leases.get(session_id)
+            return 0 if lease is None else len(lease.pages)
+
+    def holds(self, session_id: str, pages: List[int]) -> bool:
+        """Whether every page in `pages` is leased to `session_id` now (O(len(pages)))."""
+        with self._mu:
+            lease = self._leases.get(session_id)
+            return lease is not None and all(int(self._owner[p]) == lease.rank for p in pages)
 
     def touch(self, session_id: str) -> None:
         with self._mu:
@@ -354,6 +414,37 @@ class PagedSessionView:
             imp[:self._n_tokens] = self._imp[:self._n_tokens]
             self._pos, self._imp = pos, imp
 
+    def _reserve(self, n_new: int):
+        """The allocation half of push (the caller holds the lock): pages for
+        n_new more tokens, allocated in one call, in the reference's order.
+        Returns (start, fit, err): tokens start .. start + fit - 1 fit the pages
+        now held; err is the allocation error push raises once they are written."""
+        start = self._n_tokens
+        room = len(self._pages) * PAGE_SIZE - start
+        need = max(0, -(-(n_new - room) // PAGE_SIZE)) if n_new > room else 0
+        got, err = self._alloc.allocate_pages(self.session_id, need) if need else ([], None)
+        self._pages.extend(got)
+        fit = max(0, min(n_new, len(self._pages) * PAGE_SIZE - start))
+        return start, fit, err
+
+    def _record(self, start: int, fit: int, positions: List[int], importance: List[float]) -> None:
+        """The token metadata of a push's written tokens; missing positions
+        continue the token count, missing importance values are 0."""
+        if fit <= 0:
+            return
+        self._grow(start + fit)
+        idx = np.arange(fit)
+        given = np.asarray(positions[:fit], dtype=np.int64)
+        self._pos[start:start + fit] = np.where(idx < given.shape[0], np.pad(given, (0, fit - given.shape[0])),
+                                                start + idx)
+        vals = np.asarray(importance[:fit], dtype=np.float64)
+        self._imp[start:start + fit] = np.pad(vals, (0, fit - vals.shape[0]))
+        self._n_tokens = start + fit
+
+    def _commit(self) -> None:
+        self._alloc.set_token_count(self.session_id, self._n_tokens)
+        self._alloc.touch(self.session_id)
+
     def push(self, k_states: torch.Tensor, v_states: torch.Tensor, positions: List[int],
              importance: List[float]) -> None:
         """Write T tokens [n_layers, n_heads, T, head_dim] (paged_cache.py:330-363).
@@ -366,27 +457,13 @@ class PagedSessionView:
         """
         n_new = int(k_states.shape[2])
         with self._lock:
-            start = self._n_tokens
-            room = len(self._pages) * PAGE_SIZE - start
-            need = max(0, -(-(n_new - room) // PAGE_SIZE)) if n_new > room else 0
-            got, err = self._alloc.allocate_pages(self.session_id, need) if need else ([], None)
-            self._pages.extend(got)
-            fit = min(n_new, len(self._pages) * PAGE_SIZE - start)
+            start, fit, err = self._reserve(n_new)
             if fit > 0:
                 self._pool.write_rows(self._device_pages(), start, k_states[:, :, :fit], v_states[:, :, :fit])
-                self._grow(start + fit)
-                idx = np.arange(fit)
-                given = np.asarray(positions[:fit], dtype=np.int64)
-                self._pos[start:start + fit] = np.where(idx < given.shape[0],
-                                                        np.pad(given, (0, fit - given.shape[0])),
-                                                        start + idx)
-                vals = np.asarray(importance[:fit], dtype=np.float64)
-                self._imp[start:start + fit] = np.pad(vals, (0, fit - vals.shape[0]))
-                self._n_tokens = start + fit
+            self._record(start, fit, positions, importance)
             if err is not None:
                 raise err
-            self._alloc.set_token_count(self.session_id, self._n_tokens)
-            self._alloc.touch(self.session_id)
+            self._commit()
 
     def gather(self, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
         return self._pool.gather_session(layer, self._device_pages(), self._n_tokens)
@@ -453,6 +530,53 @@ class MultiSessionCache:
     def reset_all(self) -> None:
         for sid in self.sessions():
             self.reset(sid)
+
+    def push_many(self, session_ids: List[str], k_states, v_states) -> List[Optional[Exception]]:
+        """PagedSessionView.push of k_states[i], v_states[i] ([n_layers,
+        n_heads, T, head_dim]) to session_ids[i] for every i, positions and
+        importance left to their defaults, with the writes in one launch per
+        IC_PAGE_BATCH_MAX sessions.  The allocator sees exactly the calls of
+        consecutive push calls in list order (allocation, token count, touch);
+        a session whose pages a later allocation of the same call evicted is
+        not written, as its rows may already belong to another session (a
+        write goes ahead only when every page it touches is still leased to its
+        session, which keeps the call's writes on disjoint rows).  Returns the
+        error each push would have raised (None when it completed)."""
+        if len(set(session_ids)) != len(session_ids):
+            raise ValueError("push_many: a session may appear once per call")
+        views = [self.get_or_create(sid) for sid in session_ids]
+        errors: List[Optional[Exception]] = []
+        writes = []
+        with contextlib.ExitStack() as locks:
+            for view in sorted(views, key=lambda x: x.session_id):
+                locks.enter_context(view._lock)
+            for i, view in enumerate(views):
+                k, v = k_states[i], v_states[i]
+                start, fit, err = view._reserve(int(k.shape[2]))
+                if fit > 0:
+                    writes.append((view, start, k[:, :, :fit], v[:, :, :fit]))
+                view._record(start, fit, [], [])
+                if err is None:
+                    view._commit()
+                errors.append(err)
+            live = []
+            for vw, start, k, v in writes:
+                touched = vw._pages[start // PAGE_SIZE:(start + int(k.shape[2]) - 1) // PAGE_SIZE + 1]
+                if self.allocator.holds(vw.session_id, touched):
+                    live.append((vw._device_pages(), start, k, v))
+            self._pool.write_rows_many(live)
+        return errors
+
+    def gather_many(self, session_ids: List[str]) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+        """PagedSessionView.gather_all of several sessions, in one launch per
+        IC_PAGE_BATCH_MAX sessions: [(K, V)] with K, V [n_layers, n_heads,
+        n_tokens, head_dim] in list order."""
+        items = []
+        for sid in session_ids:
+            view = self.get_or_create(sid)
+            n = min(view._n_tokens, len(view._pages) * PAGE_SIZE)
+            items.append((view._device_pages(), n))
+        return self._pool.gather_rows_many(items)
 
     def sessions(self) -> List[str]:
         """Ids of every view created and not reset (with or without pages)."""

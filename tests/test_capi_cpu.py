@@ -32,7 +32,10 @@ def test_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), n
     # and the binding covers exactly the declared entry points
-    assert set(names) == set(_lib.ENTRY_POINTS) | set(_lib.INFO_ENTRY_POINTS) | set(_lib.HOST_ENTRY_POINTS)
+    assert set(names) == (set(_lib.ENTRY_POINTS) | set(_lib.BATCH_ENTRY_POINTS) | set(_lib.INFO_ENTRY_POINTS)
+                          | set(_lib.HOST_ENTRY_POINTS))
+    text = HEADER.read_text()
+    assert re.search(rf"#define IC_PAGE_BATCH_MAX {_lib.IC_PAGE_BATCH_MAX}\b", text)
 
 
 def test_status_strings():
@@ -59,11 +62,55 @@ def test_wait_probe_rejects_bad_args_without_cuda_call():
     assert lib.ic_wait_probe(ctypes.addressof(x), 3_000_000_000, None) == _lib.IC_ERR_INVALID_ARG
 
 
+def test_evict_pdl_mode_checked_without_cuda_call():
+    """ic_evict_update accepts pdl 0, 1 or 2 only; the check precedes any CUDA call."""
+    import ctypes
+    lib = _lib.load()
+    buf = (ctypes.c_int64 * 64)()
+    p = ctypes.addressof(buf)
+    sess = _lib.ic_sessions(num_sessions=1, slot_table=p, positions=p, importance=p, occupied=p, ctrl=p,
+                            counters=p)
+    for pdl in (-1, 3):
+        e = _lib.ic_evict_args(tiers=_lib.ic_tiers(sink_size=1, recent_size=2, important_size=3, budget=6),
+                               sess=sess, pdl=pdl, new_pos=p)
+        assert lib.ic_evict_update(ctypes.byref(e), None) == _lib.IC_ERR_INVALID_ARG, pdl
+
+
 def test_null_args_rejected_without_launch():
     """Argument validation runs on the host before any CUDA call."""
     lib = _lib.load()
     for name in _lib.ENTRY_POINTS:
         assert getattr(lib, name)(None, None) == _lib.IC_ERR_INVALID_ARG, name
+    for name in _lib.BATCH_ENTRY_POINTS:
+        assert getattr(lib, name)(None, 1, None) == _lib.IC_ERR_INVALID_ARG, name
+
+
+def test_page_batch_checks_without_cuda_call():
+    """Batched page gathers: the count bound, one pool and one layer range for
+    every descriptor, all checked before any CUDA call."""
+    import ctypes
+    lib = _lib.load()
+    buf = (ctypes.c_int64 * 256)()
+    p = ctypes.addressof(buf)
+    p = (p + 15) // 16 * 16
+    pool = _lib.ic_pool(k=p, v=p, pool_tokens=64, num_layers=2, num_kv_heads=1, head_dim=128, dtype=1)
+
+    def desc(**kw):
+        d = dict(pool=pool, page_ids=p, n_page_ids=2, layer_begin=0, layer_end=2, start_token=0, n_tokens=8,
+                 k_buf=p, v_buf=p, stride_l=128 * 8, stride_h=128 * 8, stride_t=128)
+        d.update(kw)
+        return _lib.ic_page_rows_args(**d)
+
+    for name in _lib.BATCH_ENTRY_POINTS:
+        fn = getattr(lib, name)
+        arr = (_lib.ic_page_rows_args * (_lib.IC_PAGE_BATCH_MAX + 1))(*[desc() for _ in range(_lib.IC_PAGE_BATCH_MAX + 1)])
+        assert fn(arr, 0, None) == _lib.IC_ERR_INVALID_ARG
+        assert fn(arr, _lib.IC_PAGE_BATCH_MAX + 1, None) == _lib.IC_ERR_INVALID_ARG
+        other = _lib.ic_pool(k=p + 16, v=p, pool_tokens=64, num_layers=2, num_kv_heads=1, head_dim=128, dtype=1)
+        for bad in (desc(pool=other), desc(layer_end=1), desc(n_tokens=-1), desc(n_tokens=40),
+                    desc(stride_t=100)):
+            two = (_lib.ic_page_rows_args * 2)(desc(), bad)
+            assert fn(two, 2, None) == _lib.IC_ERR_INVALID_ARG, name
 
 
 def test_struct_layout_matches_c():

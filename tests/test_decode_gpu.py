@@ -562,6 +562,60 @@ def test_paged_trace_gpu(golden):
     assert np.array_equal(np.concatenate(gathers), g["gathers"])
 
 
+def test_batched_page_push_and_gather_match_per_session_calls():
+    """MultiSessionCache.push_many / gather_many (one launch per 32 sessions)
+    against push / gather_all session by session on a second pool: the same
+    allocator state and gathered bytes after every call, over 40 sessions (two
+    launches per call), empty pushes and sessions, and one-token decode pushes.
+    The prompts overfill the pool, so later sessions of the first call evict
+    earlier ones (already pushed in that call); a third of the rest then leave,
+    so the decode calls evict nobody (a session evicted before its own push in
+    the same call would write stale pages in the per-session loop)."""
+    from infercache_b200 import MultiSessionCache, PagePool, PagedCacheConfig
+    rng = np.random.default_rng(11)
+
+    def make():
+        cfg = PagedCacheConfig(n_pages=160, n_layers=3, n_heads=2, head_dim=128, dtype=torch.float16,
+                               device="cuda:0", max_pages_per_session=12)
+        ticks = iter(range(1, 10 ** 6))
+        return MultiSessionCache(PagePool(cfg), clock=lambda: float(next(ticks)))
+
+    seq, bat = make(), make()
+    sids = [f"s{i}" for i in range(40)]
+    g = torch.Generator(device="cuda:0").manual_seed(5)
+    for call in range(8):
+        lens = [0 if i == 3 else (int(rng.integers(40, 120)) if call == 0 else int(rng.integers(0, 3)))
+                for i in range(len(sids))]
+        ks = [torch.randn(3, 2, n, 128, generator=g, device="cuda:0").half() for n in lens]
+        vs = [torch.randn(3, 2, n, 128, generator=g, device="cuda:0").half() for n in lens]
+        errs = []
+        for sid, k, v in zip(sids, ks, vs):
+            try:
+                seq.get_or_create(sid).push(k, v, positions=[], importance=[])
+                errs.append(None)
+            except RuntimeError as e:
+                errs.append(str(e))
+        got = [None if e is None else str(e) for e in bat.push_many(sids, ks, vs)]
+        assert got == errs, call
+        assert seq.allocator.free_list() == bat.allocator.free_list(), call
+        live = [sid for sid in sids if seq.allocator.pages_for(sid)]
+        for sid in sids:
+            assert seq.allocator.pages_for(sid) == bat.allocator.pages_for(sid), (call, sid)
+        many = bat.gather_many(live)
+        for sid, (K, V) in zip(live, many):
+            K0, V0 = seq.get_or_create(sid).gather_all()
+            assert torch.equal(K, K0) and torch.equal(V, V0), (call, sid)
+        gone = [s_ for s_ in sids if s_ not in live] + (live[::3] if call == 0 else [])
+        for sid in gone:  # evicted sessions start again, as the stress workload's do
+            seq.reset(sid)
+            bat.reset(sid)
+        if call == 0:
+            evictions = bat.allocator.lru_evictions
+            assert evictions > 0
+    assert bat.allocator.lru_evictions == evictions
+    torch.cuda.synchronize()
+
+
 def _random_spec(i):
     r = np.random.default_rng(1000 + i)
     hkv = int(r.integers(1, 3))

@@ -23,6 +23,10 @@ class RecordingPool:
     def write_rows(self, page_ids, start_token, k, v, layer_begin=0):
         self.writes.append((list(page_ids), start_token, k.shape[2]))
 
+    def write_rows_many(self, items):
+        for page_ids, start_token, k, v in items:
+            self.writes.append((list(page_ids), start_token, k.shape[2]))
+
     def gather_session(self, layer, page_ids, n_tokens):
         return None, None
 
@@ -183,6 +187,9 @@ class _GatherPool(RecordingPool):
         K = torch.empty(layer_end - layer_begin, c.n_heads, n_tokens, c.head_dim, device="meta")
         return K, K
 
+    def gather_rows_many(self, items):
+        return [self.gather_rows(p, n, 0, self.cfg.n_layers) for p, n in items]
+
 
 def test_paged_stress_host_logic_matches_oracle_allocator():
     """The config-5 driver (bench.paged_stress) on the host with a recording
@@ -211,3 +218,90 @@ def test_paged_stress_host_logic_matches_oracle_allocator():
     assert 0.0 <= r["fragmentation_mean"] <= r["fragmentation_max"] < 1.0
     assert bench.replay_on_oracle(rec.ops, 60, 30, rec.inner.free_list())
     assert msc.allocator.free_pages() == 60  # every session departed or was dropped
+
+
+def _small_msc(n_pages, max_pps):
+    cfg = PagedCacheConfig(n_pages=n_pages, n_layers=1, n_heads=1, head_dim=8, dtype=torch.float32, device="cpu",
+                           max_pages_per_session=max_pps)
+    ticks = iter(range(1, 10 ** 6))
+    return MultiSessionCache(RecordingPool(cfg), clock=lambda: float(next(ticks)))
+
+
+def test_push_many_matches_consecutive_pushes():
+    """push_many makes the allocator calls of consecutive pushes in list order:
+    the same pages, free list, token counts, LRU victims and errors after every
+    call; its writes are those of the pushes, less the ones whose pages were
+    evicted by a later allocation of the same call."""
+    rng = np.random.default_rng(7)
+    seq, bat = _small_msc(24, 5), _small_msc(24, 5)
+    sids = [f"s{i}" for i in range(7)]
+    for call in range(30):
+        pick = list(rng.choice(sids, size=int(rng.integers(1, 6)), replace=False))
+        lens = [int(rng.integers(0, 40)) for _ in pick]
+        ks = [torch.zeros(1, 1, n, 8) for n in lens]
+        errs_seq = []
+        for sid, k in zip(pick, ks):
+            try:
+                seq.get_or_create(sid).push(k, k, positions=[], importance=[])
+                errs_seq.append(None)
+            except RuntimeError as e:
+                errs_seq.append(str(e))
+        errs_bat = [None if e is None else str(e) for e in bat.push_many(pick, ks, ks)]
+        assert errs_bat == errs_seq, call
+        assert seq.allocator.free_list() == bat.allocator.free_list(), call
+        for sid in sids:
+            assert seq.allocator.pages_for(sid) == bat.allocator.pages_for(sid), (call, sid)
+            assert seq.allocator.get_token_count(sid) == bat.allocator.get_token_count(sid)
+            assert seq.get_or_create(sid).n_tokens == bat.get_or_create(sid).n_tokens
+        assert seq.allocator.lru_evictions == bat.allocator.lru_evictions
+        if rng.random() < 0.2:
+            gone = str(rng.choice(sids))
+            seq.reset(gone)
+            bat.reset(gone)
+    assert seq.allocator.lru_evictions > 0
+    # every batched write is one of the consecutive pushes' writes, on pages leased at the time
+    assert set(map(lambda w: (tuple(w[0]), w[1], w[2]), bat._pool.writes)) <= \
+        set(map(lambda w: (tuple(w[0]), w[1], w[2]), seq._pool.writes))
+
+
+def test_push_many_skips_writes_to_pages_evicted_in_the_same_call():
+    """Two sessions hold four of five pages; in one push_many call the first
+    appends into its last page, then the second takes the free page (which
+    makes it the most recently used) and, for a second page, evicts the first:
+    the first session's write is dropped, the second's kept."""
+    msc = _small_msc(5, 4)
+    z = torch.zeros(1, 1, 24, 8)
+    msc.push_many(["A", "B"], [z, z], [z, z])
+    assert len(msc.allocator.pages_for("A")) == 2 and len(msc.allocator.pages_for("B")) == 2
+    msc._pool.writes.clear()
+    one = torch.zeros(1, 1, 1, 8)
+    more = torch.zeros(1, 1, 25, 8)
+    errs = msc.push_many(["A", "B"], [one, more], [one, more])
+    assert errs == [None, None]
+    assert msc.allocator.pages_for("A") == [] and msc.allocator.lru_evictions == 1
+    assert len(msc.allocator.pages_for("B")) == 4
+    assert [w[1:] for w in msc._pool.writes] == [(24, 25)]
+
+
+def test_push_many_rejects_repeated_sessions():
+    msc = _small_msc(4, 4)
+    z = torch.zeros(1, 1, 1, 8)
+    with pytest.raises(ValueError):
+        msc.push_many(["A", "A"], [z, z], [z, z])
+
+
+def test_allocator_page_count_and_holds():
+    ticks = iter(range(1, 100))
+    a = KVAllocator(4, 3, clock=lambda: float(next(ticks)))
+    a.allocate_page("x")
+    a.allocate_page("x")
+    a.allocate_page("y")
+    assert a.page_count("x") == 2 and a.page_count("y") == 1 and a.page_count("z") == 0
+    assert a.holds("x", a.pages_for("x")) and not a.holds("x", a.pages_for("y")) and a.holds("x", [])
+    a.touch("x")
+    a.allocate_page("z")
+    gone = a.pages_for("y")
+    a.allocate_page("z")                     # evicts y; its page goes to z
+    assert not a.holds("y", gone) and a.holds("z", gone) and a.page_count("y") == 0
+    a.release_session("x")
+    assert not a.holds("x", [3]) and a.page_count("x") == 0
