@@ -521,7 +521,8 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
     into HF layout (to_hf_past_key_values, paged_cache.py:365-378) -- and
     depart (reset).  A tick serves every active session once, the pushes and
     gathers of its sessions batched (MultiSessionCache.push_many /
-    gather_many, up to 32 sessions and 2 GiB of output per gather launch); its duration is
+    gather_many, up to 32 sessions per launch, the gathers into a reused 2 GiB
+    output arena); its duration is
     `tick_timer(fn)` (device time around fn) and advances the clock.  When the
     pool runs out, the allocator evicts the least recently used session; a
     session that lost its pages that way is dropped.  Returns counters and the
@@ -539,8 +540,15 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
     alloc = msc.allocator
     tok_k, tok_v = src_k[:, :, :1], src_v[:, :, :1]
     from infercache_b200 import _lib
-    row_bytes = src_k.shape[0] * src_k.shape[1] * src_k.shape[3] * src_k.element_size()  # one token, all layers
-    gather_budget = 2 << 30  # output bytes of one batched gather launch
+    L_, H_, D_ = src_k.shape[0], src_k.shape[1], src_k.shape[3]
+    # the gathered K/V of a batch land in one arena allocated once (2 GiB)
+    arena = torch.empty((2 << 30) // src_k.element_size(), dtype=src_k.dtype, device=src_k.device)
+
+    def flush(group, views, counts):
+        for y, (K, V) in zip(group, msc.gather_many([str(z) for z in group], views)):
+            counts["decode"] += 1
+            counts["gathered"] += 2 * 2 * K.numel() * K.element_size()  # K and V, read and written
+            active[y][1] -= 1
 
     def admit(sid, n):
         nonlocal prompt_tokens
@@ -577,23 +585,32 @@ def paged_stress(msc, trace, decode_steps, src_k, src_v, tick_timer, sample_ms=1
             # per-session cap are ignored: such a session decodes over what it
             # holds), written in one launch with the allocator calls of a
             # per-session loop, then the chunk's whole-session gathers in one
-            # launch (or more, at most gather_budget bytes of output each), so
-            # the next chunk's host work overlaps this chunk's copies
+            # launch (or more, when their outputs overflow the arena), so the
+            # next chunk's host work overlaps this chunk's copies
             step = _lib.IC_PAGE_BATCH_MAX
             for c0 in range(0, len(sids), step):
                 chunk = sids[c0:c0 + step]
                 msc.push_many([str(x) for x in chunk], [tok_k] * len(chunk), [tok_v] * len(chunk))
                 live = [x for x in chunk if alloc.page_count(str(x))]
-                group, size = [], 0
+                # outputs carved from one reused arena, 256-byte aligned
+                group, views, off = [], [], 0
                 for i, x in enumerate(live):
+                    n = msc.gathered_tokens(str(x))
+                    elems = L_ * H_ * n * D_
+                    if group and off + 2 * elems + 256 > arena.numel():
+                        flush(group, views, counts)
+                        group, views, off = [], [], 0
+                    if 2 * elems + 256 > arena.numel():  # larger than the arena: its own tensors
+                        flush([x], None, counts)
+                        continue
+                    K = arena[off:off + elems].view(L_, H_, n, D_)
+                    off = (off + elems + 127) // 128 * 128
+                    V = arena[off:off + elems].view(L_, H_, n, D_)
+                    off = (off + elems + 127) // 128 * 128
                     group.append(x)
-                    size += 2 * active[x][0].n_tokens * row_bytes
-                    if size >= gather_budget or i == len(live) - 1:
-                        for y, (K, V) in zip(group, msc.gather_many([str(z) for z in group])):
-                            counts["decode"] += 1
-                            counts["gathered"] += 2 * 2 * K.numel() * K.element_size()  # K and V, read and written
-                            active[y][1] -= 1
-                        group, size = [], 0
+                    views.append((K, V))
+                if group:
+                    flush(group, views, counts)
             prune()
 
         dt = tick_timer(tick)

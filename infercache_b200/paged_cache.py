@@ -169,14 +169,25 @@ class PagePool:
             descs.append(self._rows_args(pid, len(page_ids), start, k, v, 0))
         self._run_batches("ic_page_write_batch", descs)
 
-    def gather_rows_many(self, items) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+    def gather_rows_many(self, items, out=None) -> List[Tuple[torch.Tensor, torch.Tensor]]:
         """gather_rows(page_ids, n_tokens, 0, n_layers) for several page lists:
-        items are (page_ids, n_tokens); one launch per IC_PAGE_BATCH_MAX items."""
+        items are (page_ids, n_tokens); one launch per IC_PAGE_BATCH_MAX items.
+        `out`, if given, holds a (K, V) pair per item to gather into: tensors of
+        the pool's dtype and device, shape [n_layers, n_heads, n_tokens,
+        head_dim], rows contiguous and 16-byte aligned."""
         c = self.cfg
         outs, descs = [], []
-        for page_ids, n in items:
-            K = torch.empty(c.n_layers, c.n_heads, n, c.head_dim, dtype=c.dtype, device=self.device)
-            V = torch.empty_like(K)
+        for i, (page_ids, n) in enumerate(items):
+            if out is None:
+                K = torch.empty(c.n_layers, c.n_heads, n, c.head_dim, dtype=c.dtype, device=self.device)
+                V = torch.empty_like(K)
+            else:
+                K, V = out[i]
+                shape = (c.n_layers, c.n_heads, n, c.head_dim)
+                for x in (K, V):
+                    if tuple(x.shape) != shape or x.dtype != c.dtype or x.device != self.device or x.stride(-1) != 1:
+                        raise ValueError(f"gather_rows_many: out[{i}] must be {shape} {c.dtype} on {self.device} "
+                                         "with contiguous rows")
             outs.append((K, V))
             if n > 0:
                 descs.append(self._rows_args(self._page_ids(page_ids), len(page_ids), 0, K, V, 0))
@@ -237,6 +248,9 @@ class KVAllocator:
     def _stamp(self, session_id: str, lease: _Lease) -> None:
         lease.stamp = self._now()
         heapq.heappush(self._lru, (lease.stamp, lease.rank, session_id))
+        if len(self._lru) > 4 * len(self._leases) + 64:  # drop stale heap entries now and then
+            self._lru = [(lz.stamp, lz.rank, sid) for sid, lz in self._leases.items()]
+            heapq.heapify(self._lru)
 
     def _drop(self, session_id: str) -> None:
         lease = self._leases.pop(session_id, None)
@@ -273,9 +287,6 @@ class KVAllocator:
         lease.pages.append(page)
         self._owner[page] = lease.rank
         self._stamp(session_id, lease)
-        if len(self._lru) > 4 * len(self._leases) + 64:  # drop stale heap entries now and then
-            self._lru = [(lz.stamp, lz.rank, sid) for sid, lz in self._leases.items()]
-            heapq.heapify(self._lru)
         return page
 
     # -- the reference's interface -------------------------------------------------------
@@ -291,7 +302,26 @@ class KVAllocator:
         the pages obtained before any failure, and that failure (or None)."""
         got: List[int] = []
         with self._mu:
-            for _ in range(count):
+            while len(got) < count:
+                # pages that need neither an eviction nor pass the cap come off
+                # the stack in one slice (the order consecutive takes give) with
+                # one stamp: no victim is chosen in between, so the intermediate
+                # stamps could not change any decision; the others one by one
+                lease = self._leases.get(session_id)
+                have = 0 if lease is None else len(lease.pages)
+                fast = min(count - len(got), self.max_pages_per_session - have, self._top)
+                if fast > 0:
+                    if lease is None:
+                        lease = self._leases[session_id] = _Lease(rank=self._next_rank)
+                        self._next_rank += 1
+                    pages = self._stack[self._top - fast:self._top][::-1]
+                    self._top -= fast
+                    self._owner[pages] = lease.rank
+                    taken = pages.tolist()
+                    lease.pages.extend(taken)
+                    got.extend(taken)
+                    self._stamp(session_id, lease)
+                    continue
                 try:
                     got.append(self._take(session_id))
                 except RuntimeError as e:
@@ -306,6 +336,8 @@ class KVAllocator:
 
     def holds(self, session_id: str, pages: List[int]) -> bool:
         """Whether every page in `pages` is leased to `session_id` now (O(len(pages)))."""
+        if len(pages) == 0:
+            return True
         with self._mu:
             lease = self._leases.get(session_id)
             return lease is not None and all(int(self._owner[p]) == lease.rank for p in pages)
@@ -433,12 +465,11 @@ class PagedSessionView:
         if fit <= 0:
             return
         self._grow(start + fit)
-        idx = np.arange(fit)
-        given = np.asarray(positions[:fit], dtype=np.int64)
-        self._pos[start:start + fit] = np.where(idx < given.shape[0], np.pad(given, (0, fit - given.shape[0])),
-                                                start + idx)
-        vals = np.asarray(importance[:fit], dtype=np.float64)
-        self._imp[start:start + fit] = np.pad(vals, (0, fit - vals.shape[0]))
+        npos, nimp = min(len(positions), fit), min(len(importance), fit)
+        self._pos[start:start + npos] = np.asarray(positions[:npos], dtype=np.int64)
+        self._pos[start + npos:start + fit] = np.arange(start + npos, start + fit, dtype=np.int64)
+        self._imp[start:start + nimp] = np.asarray(importance[:nimp], dtype=np.float64)
+        self._imp[start + nimp:start + fit] = 0.0
         self._n_tokens = start + fit
 
     def _commit(self) -> None:
@@ -567,16 +598,22 @@ class MultiSessionCache:
             self._pool.write_rows_many(live)
         return errors
 
-    def gather_many(self, session_ids: List[str]) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+    def gather_many(self, session_ids: List[str], out=None) -> List[Tuple[torch.Tensor, torch.Tensor]]:
         """PagedSessionView.gather_all of several sessions, in one launch per
         IC_PAGE_BATCH_MAX sessions: [(K, V)] with K, V [n_layers, n_heads,
-        n_tokens, head_dim] in list order."""
+        n_tokens, head_dim] in list order (written into `out`'s pairs when
+        given: see PagePool.gather_rows_many)."""
         items = []
         for sid in session_ids:
             view = self.get_or_create(sid)
             n = min(view._n_tokens, len(view._pages) * PAGE_SIZE)
             items.append((view._device_pages(), n))
-        return self._pool.gather_rows_many(items)
+        return self._pool.gather_rows_many(items, out)
+
+    def gathered_tokens(self, session_id: str) -> int:
+        """The token count gather_all / gather_many return for `session_id`."""
+        view = self.get_or_create(session_id)
+        return min(view._n_tokens, len(view._pages) * PAGE_SIZE)
 
     def sessions(self) -> List[str]:
         """Ids of every view created and not reset (with or without pages)."""

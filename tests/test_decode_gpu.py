@@ -602,6 +602,18 @@ def test_batched_page_push_and_gather_match_per_session_calls():
         for sid in sids:
             assert seq.allocator.pages_for(sid) == bat.allocator.pages_for(sid), (call, sid)
         many = bat.gather_many(live)
+        if call % 2:  # into caller buffers carved from one flat tensor
+            flat = torch.full((sum(2 * K.numel() + 128 for K, _ in many),), 7.0, dtype=torch.float16,
+                              device="cuda:0")
+            outs, off = [], 0
+            for K, _ in many:
+                pair = []
+                for _ in range(2):
+                    pair.append(flat[off:off + K.numel()].view(K.shape))
+                    off = (off + K.numel() + 63) // 64 * 64
+                outs.append(tuple(pair))
+            many = bat.gather_many(live, out=outs)
+            assert all(a is b for pr, pb in zip(many, outs) for a, b in zip(pr, pb))
         for sid, (K, V) in zip(live, many):
             K0, V0 = seq.get_or_create(sid).gather_all()
             assert torch.equal(K, K0) and torch.equal(V, V0), (call, sid)

@@ -187,7 +187,9 @@ class _GatherPool(RecordingPool):
         K = torch.empty(layer_end - layer_begin, c.n_heads, n_tokens, c.head_dim, device="meta")
         return K, K
 
-    def gather_rows_many(self, items):
+    def gather_rows_many(self, items, out=None):
+        if out is not None:
+            return out
         return [self.gather_rows(p, n, 0, self.cfg.n_layers) for p, n in items]
 
 
@@ -305,3 +307,43 @@ def test_allocator_page_count_and_holds():
     assert not a.holds("y", gone) and a.holds("z", gone) and a.page_count("y") == 0
     a.release_session("x")
     assert not a.holds("x", [3]) and a.page_count("x") == 0
+
+
+def test_allocate_pages_matches_consecutive_allocate_page_on_oracle():
+    """allocate_pages (free pages taken in slices between evictions) against
+    the oracle's allocate_page called count times: the same pages in the same
+    order, the same error at the same point, the same free stack and holders,
+    over random counts that cross the per-session cap and empty the pool."""
+    import random
+    from oracle.paged import OracleAllocator
+    rng = random.Random(9)
+    for trial in range(30):
+        n_pages, cap = rng.randint(1, 40), rng.randint(1, 12)
+        oa = OracleAllocator(n_pages, cap)
+        ticks = iter(range(1, 10 ** 6))
+        ka = KVAllocator(n_pages, cap, clock=lambda: float(next(ticks)))
+        sids = [f"s{i}" for i in range(rng.randint(1, 5))]
+        for step in range(200):
+            sid, r = rng.choice(sids), rng.random()
+            if r < 0.6:
+                count = rng.randint(0, 15)
+                want, werr = [], ""
+                for _ in range(count):
+                    try:
+                        want.append(oa.allocate_page(sid))
+                    except RuntimeError as e:
+                        werr = str(e)
+                        break
+                got, err = ka.allocate_pages(sid, count)
+                assert (got, str(err) if err else "") == (want, werr), (trial, step)
+            elif r < 0.8:
+                oa.touch(sid)
+                ka.touch(sid)
+            else:
+                oa._release(sid)
+                ka.release_session(sid)
+            assert ka.free_list() == oa.free, (trial, step)
+            assert ka.active_sessions() == list(oa.pages), (trial, step)
+            for x in sids:
+                assert ka.pages_for(x) == oa.pages.get(x, [])
+                assert ka.holds(x, ka.pages_for(x))
