@@ -551,6 +551,14 @@ int ic_host_device_pointer(const void* host, void** device);
  * counterpart (the reference has no device-side waits). */
 int ic_wait_probe(int32_t* dev_status, int64_t limit_ns, void* stream);
 
+/* ---- graph replay loop -----------------------------------------------------
+ * `rounds` times, for i < n: cudaGraphLaunch(execs[i], streams[i]) (execs are
+ * cudaGraphExec_t, streams cudaStream_t, as void*).  A host loop of many small
+ * graph launches -- one per session range and step in a grouped host stepper
+ * -- then costs no interpreter call per launch.  No reference counterpart (the
+ * reference launches every kernel from Python). */
+int ic_graph_replay(void* const* execs, void* const* streams, int32_t n, int32_t rounds);
+
 /* ---- library information --------------------------------------------------*/
 const char* ic_status_str(int status);
 int ic_abi_version(void);

@@ -219,7 +219,7 @@ BATCH_ENTRY_POINTS = {
 }
 IC_PAGE_BATCH_MAX = 32
 INFO_ENTRY_POINTS = ["ic_status_str", "ic_abi_version", "ic_device_check", "ic_last_error"]
-HOST_ENTRY_POINTS = ["ic_host_device_pointer", "ic_wait_probe"]
+HOST_ENTRY_POINTS = ["ic_host_device_pointer", "ic_wait_probe", "ic_graph_replay"]
 
 _LIB = None
 
@@ -253,6 +253,8 @@ def load(path: Path = LIB_PATH):
     lib.ic_host_device_pointer.restype = c_int
     lib.ic_wait_probe.argtypes = [c_void_p, c_int64, c_void_p]
     lib.ic_wait_probe.restype = c_int
+    lib.ic_graph_replay.argtypes = [POINTER(c_void_p), POINTER(c_void_p), c_int32, c_int32]
+    lib.ic_graph_replay.restype = c_int
     _LIB = lib
     return lib
 

@@ -95,3 +95,27 @@ extern "C" int ic_wait_probe(int32_t* dev_status, int64_t limit_ns, void* stream
   wait_probe_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(dev_status, static_cast<uint64_t>(limit_ns));
   return ic::launch_status("wait_probe");
 }
+
+extern "C" int ic_graph_replay(void* const* execs, void* const* streams, int32_t n, int32_t rounds) {
+  if (!execs || !streams || n < 1 || n > 4096 || rounds < 0) {
+    ic::set_last_error("graph_replay: execs and streams required, 1 <= n <= 4096, rounds >= 0");
+    return IC_ERR_INVALID_ARG;
+  }
+  for (int32_t i = 0; i < n; ++i) {
+    if (!execs[i]) {
+      ic::set_last_error("graph_replay: null graph");
+      return IC_ERR_INVALID_ARG;
+    }
+  }
+  for (int32_t r = 0; r < rounds; ++r) {
+    for (int32_t i = 0; i < n; ++i) {
+      const cudaError_t e = cudaGraphLaunch(static_cast<cudaGraphExec_t>(execs[i]),
+                                            static_cast<cudaStream_t>(streams[i]));
+      if (e != cudaSuccess) {
+        ic::set_last_error(cudaGetErrorString(e));
+        return IC_ERR_LAUNCH;
+      }
+    }
+  }
+  return IC_OK;
+}

@@ -209,6 +209,27 @@ __device__ __forceinline__ void warp_argmin(float& v, int& i) {
     if (argmin_less(ov, oi, v, i)) { v = ov; i = oi; }
   }
 }
+// The argmin (v, i) as above together with r, the fminf of every other value
+// (the runner-up; NaN values are skipped as fminf skips them).  Every lane
+// ends with the same triple.
+__device__ __forceinline__ void argmin2_take(float& v, int& i, float& r, float ov, int oi, float orr) {
+  if (argmin_less(ov, oi, v, i)) {
+    r = fminf(fminf(r, orr), v);
+    v = ov;
+    i = oi;
+  } else {
+    r = fminf(fminf(r, orr), ov);
+  }
+}
+__device__ __forceinline__ void warp_argmin2(float& v, int& i, float& r) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(FULL_MASK, v, o);
+    const int oi = __shfl_xor_sync(FULL_MASK, i, o);
+    const float orr = __shfl_xor_sync(FULL_MASK, r, o);
+    argmin2_take(v, i, r, ov, oi, orr);
+  }
+}
 
 // ---- host-side status plumbing ----------------------------------------------
 void set_last_error(const char* msg);

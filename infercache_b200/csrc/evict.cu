@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   extern __shared__ __align__(16) unsigned char ev_smem[];
   __shared__ float red_v[EV_THREADS / 32];
   __shared__ int red_i[EV_THREADS / 32];
+  __shared__ float red_r[EV_THREADS / 32];
   __shared__ int amin_slot;
   __shared__ float runner_up;
 
@@ -175,36 +176,28 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   const float score = imp_s[r];
   const bool need_argmin = displaced && !(score <= 0.f) && l2fill >= cap && cap > 0;
 
-  // 2. first-index argmin over the filled L2 slice
+  // 2. first-index argmin over the filled L2 slice, and the smallest other
+  // score (the runner-up, to count decisions that rest on a near-tie), in one
+  // pass and one block reduction
   if (need_argmin) {
     float bv = __int_as_float(0x7f800000);  // +inf
     int bi = 0x7fffffff;
-    for (int j = l2s + tid; j < l2s + l2fill; j += EV_THREADS) {
-      const float v = imp_s[j];
-      if (argmin_less(v, j, bv, bi)) { bv = v; bi = j; }
-    }
-    warp_argmin(bv, bi);
-    if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; }
-    __syncthreads();
-    if (warp == 0) {
-      bv = lane < EV_THREADS / 32 ? red_v[lane] : __int_as_float(0x7f800000);
-      bi = lane < EV_THREADS / 32 ? red_i[lane] : 0x7fffffff;
-      warp_argmin(bv, bi);
-      if (lane == 0) amin_slot = bi;
-    }
-    __syncthreads();
-    // the runner-up score, to count decisions that rest on a near-tie
     float sv = __int_as_float(0x7f800000);
     for (int j = l2s + tid; j < l2s + l2fill; j += EV_THREADS)
-      if (j != amin_slot) sv = fminf(sv, imp_s[j]);
-    sv = warp_min(sv);
-    __syncthreads();  // red_v is reused
-    if (lane == 0) red_v[warp] = sv;
+      argmin2_take(bv, bi, sv, imp_s[j], j, __int_as_float(0x7f800000));
+    warp_argmin2(bv, bi, sv);
+    if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; red_r[warp] = sv; }
     __syncthreads();
     if (warp == 0) {
-      sv = lane < EV_THREADS / 32 ? red_v[lane] : __int_as_float(0x7f800000);
-      sv = warp_min(sv);
-      if (lane == 0) runner_up = sv;
+      const bool has = lane < EV_THREADS / 32;
+      bv = has ? red_v[lane] : __int_as_float(0x7f800000);
+      bi = has ? red_i[lane] : 0x7fffffff;
+      sv = has ? red_r[lane] : __int_as_float(0x7f800000);
+      warp_argmin2(bv, bi, sv);
+      if (lane == 0) {
+        amin_slot = bi;
+        runner_up = sv;
+      }
     }
     __syncthreads();
   }

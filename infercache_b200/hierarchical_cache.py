@@ -36,6 +36,7 @@ library.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import List, Optional, Sequence, Tuple
 
@@ -598,6 +599,7 @@ class GroupedStepper:
         dev = batch.device
         self.streams = [torch.cuda.Stream(device=dev) for _ in self.ranges]
         self.graphs = []
+        self._replay = None
         cap = torch.cuda.Stream(device=dev)
         cap.wait_stream(torch.cuda.current_stream(dev))
         for a in self._args:
@@ -618,12 +620,31 @@ class GroupedStepper:
         cur = torch.cuda.current_stream(self.batch.device)
         for s in self.streams:
             s.wait_stream(cur)
-        for _ in range(int(replays)):
-            for s, g in zip(self.streams, self.graphs):
-                with torch.cuda.stream(s):
-                    g.replay()
+        if self._replay is None:
+            self._replay = _GraphReplay(self.graphs, self.streams)
+        self._replay(int(replays))
         for s in self.streams:
             cur.wait_stream(s)
+
+
+class _GraphReplay:
+    """Replays CUDA graphs, graph i on stream i, `rounds` times over, in one
+    library call (ic_graph_replay): a grouped stepper's many small launches
+    then cost no interpreter call each.  Holds the graphs, so their
+    executables stay alive."""
+
+    def __init__(self, graphs, streams) -> None:
+        self.graphs, self.streams = list(graphs), list(streams)
+        n = len(self.graphs)
+        self._execs = (ctypes.c_void_p * n)(*[int(g.raw_cuda_graph_exec()) for g in self.graphs])
+        self._strms = (ctypes.c_void_p * n)(*[int(st.cuda_stream) for st in self.streams])
+
+    def __call__(self, rounds: int) -> None:
+        if rounds <= 0:
+            return
+        lib = _lib.load()
+        _lib.raise_for(lib.ic_graph_replay(self._execs, self._strms, len(self.graphs), int(rounds)),
+                       "ic_graph_replay")
 
 
 class GroupedHostStepper:
@@ -666,6 +687,7 @@ class GroupedHostStepper:
         self._dev = []
         self.streams = [torch.cuda.Stream(device=dev) for _ in self.ranges]
         self.graphs = []
+        self._replay = None
         self.h2d_bytes = self.d2h_bytes = 0
         cap = torch.cuda.Stream(device=dev)
         cap.wait_stream(torch.cuda.current_stream(dev))
@@ -721,10 +743,9 @@ class GroupedHostStepper:
         cur = torch.cuda.current_stream(self.batch.device)
         for s in self.streams:
             s.wait_stream(cur)
-        for _ in range(int(steps)):
-            for s, g in zip(self.streams, self.graphs):
-                with torch.cuda.stream(s):
-                    g.replay()
+        if self._replay is None:
+            self._replay = _GraphReplay(self.graphs, self.streams)
+        self._replay(int(steps))
         for s in self.streams:
             cur.wait_stream(s)
 

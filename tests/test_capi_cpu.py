@@ -62,6 +62,19 @@ def test_wait_probe_rejects_bad_args_without_cuda_call():
     assert lib.ic_wait_probe(ctypes.addressof(x), 3_000_000_000, None) == _lib.IC_ERR_INVALID_ARG
 
 
+def test_graph_replay_rejects_bad_args_without_cuda_call():
+    import ctypes
+    lib = _lib.load()
+    arr = (ctypes.c_void_p * 2)(1, 2)
+    nul = (ctypes.c_void_p * 2)(1, None)
+    assert lib.ic_graph_replay(None, arr, 2, 1) == _lib.IC_ERR_INVALID_ARG
+    assert lib.ic_graph_replay(arr, None, 2, 1) == _lib.IC_ERR_INVALID_ARG
+    assert lib.ic_graph_replay(arr, arr, 0, 1) == _lib.IC_ERR_INVALID_ARG
+    assert lib.ic_graph_replay(arr, arr, 2, -1) == _lib.IC_ERR_INVALID_ARG
+    assert lib.ic_graph_replay(nul, arr, 2, 1) == _lib.IC_ERR_INVALID_ARG
+    assert lib.ic_graph_replay(arr, arr, 2, 0) == _lib.IC_OK  # nothing to launch
+
+
 def test_evict_pdl_mode_checked_without_cuda_call():
     """ic_evict_update accepts pdl 0, 1 or 2 only; the check precedes any CUDA call."""
     import ctypes
