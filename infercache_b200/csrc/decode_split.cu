@@ -14,23 +14,22 @@
 //      scores start as soon as K has landed); slots past the last are zero
 //      rows; the staging slot (the token being decoded) takes k_new / v_new,
 //      which the CTA also writes to the pool.  With programmatic dependent
-//      launch, layers after the first issue the K copies before waiting for
-//      the previous kernel (it does not write this layer's pool rows), then
-//      load q, then issue the V copies;
+//      launch, layers after the first issue these copies before waiting for the
+//      previous kernel: it does not write this layer's pool rows;
 //   2. S^T = K . Q^T on the tensor cores (mma.sync m16n8k16, the warp's K rows
 //      as A through ldmatrix, the group's query heads as B in registers), the
 //      warp's exact per-head maximum, P = 2^(s - max);
 //   3. O^T = V^T . P^T (V rows transposed by ldmatrix.trans, the S^T fragment
 //      turned into the P^T operand by movmatrix.trans);
 //   4. the warps merge into the CTA's per-head (max, sum, O);
-//   5. the cluster merges in one exchange, without a cluster-wide barrier on
-//      the way: every CTA pushes its (max, sum) pairs into every peer's shared
-//      memory and slice j of its O (relative to its own max) into CTA j's, all
-//      with st.async completing on the receiver's one mbarrier; once
-//      everything has arrived each CTA knows the group's softmax, scales the
-//      CL slices it received and sums them in CTA order (deterministic) into
-//      its part of `out`, and adds the received mass of its own slots (summed
-//      over the group's heads in head order) to the running sum over layers.
+//   5. the cluster merges without a cluster-wide barrier on the way: every CTA
+//      pushes its (max, sum) pairs into every peer's shared memory with
+//      st.async, completing on the peer's mbarrier; once all CL pairs have
+//      arrived each CTA knows the group's softmax, adds the received mass of
+//      its own slots (summed over the group's heads in head order) to the
+//      running sum over layers, scales its O and pushes slice j of it to CTA j;
+//      CTA j sums the CL slices it receives in CTA order (deterministic) and
+//      writes its part of `out`.
 // No global scratch and no atomics.
 #include <math.h>
 
@@ -72,7 +71,7 @@ __host__ __device__ inline SplitGeom split_geometry(int ntot, int hs, int cl_req
 }
 
 struct SplitSmem {
-  int k_off, v_off, sc_off, row_off, occ_off, stin_off, red_off, cst_off, bar_off, total, pitch, rows;
+  int k_off, v_off, sc_off, row_off, occ_off, stin_off, red_off, ocs_off, cst_off, bar_off, total, pitch, rows;
 };
 
 __host__ __device__ inline SplitSmem split_smem(const SplitGeom& g, int hs) {
@@ -87,8 +86,9 @@ __host__ __device__ inline SplitSmem split_smem(const SplitGeom& g, int hs) {
   L.occ_off = o;  o = sp_align(o + L.rows, 16);
   L.stin_off = o; o += SP_MAXCL * hs * 2 * 4;        // [CL][hs] (max, sum) from every CTA
   L.red_off = o;  o += g.cl * g.slice * 4;           // [CL][slice] O slices from every CTA
-  L.cst_off = o;  o += (2 + SP_MAXCL) * hs * 4;      // M, 1 / L, then [CL] scale per head
-  L.bar_off = o;  o += 16;                           // mbarrier: stats and O slices
+  L.ocs_off = o;  o += hs * SP_D * 4;                // this CTA's merged O [hs][128]
+  L.cst_off = o;  o += 4 * hs * 4;                   // m_cta, l_cta, M, 1 / L per head
+  L.bar_off = o;  o += 16;                           // mbarriers: stats, O slices
   L.total = o;
   return L;
 }
@@ -158,7 +158,8 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
   uint8_t* occ_s = smem + L.occ_off;
   float* stin = reinterpret_cast<float*>(smem + L.stin_off);   // [CL][HS][2]
   float* red = reinterpret_cast<float*>(smem + L.red_off);     // [CL][SL]
-  float* cst = reinterpret_cast<float*>(smem + L.cst_off);     // [2 + CL][HS]
+  float* ocs = reinterpret_cast<float*>(smem + L.ocs_off);     // [HS][SP_D]
+  float* cst = reinterpret_cast<float*>(smem + L.cst_off);     // [4][HS]
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   const int pitch = L.pitch;
   const int own0 = c * chunk;                      // first slot of this CTA
@@ -167,8 +168,10 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
 
   if (tid == 0) {
     mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_barrier_init();
-    mbar_arrive_expect_tx(&bar[0], static_cast<uint32_t>(CL * HS * 2 * 4 + CL * red_len * 4));
+    mbar_arrive_expect_tx(&bar[0], static_cast<uint32_t>(CL * HS * 2 * 4));
+    mbar_arrive_expect_tx(&bar[1], static_cast<uint32_t>(CL * red_len * 4));
   }
   // peers may push into this CTA's shared memory once every CTA has passed here
   cluster_arrive_release();
@@ -213,10 +216,12 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
   __syncwarp();
   // K rows in one commit group, V rows in a second; half-warps take a row per
   // pass (256 contiguous bytes); rows without a slot are zero (their scores are
-  // masked; V must be finite).  q is loaded between the two, so its load does
-  // not queue behind the V copies.
+  // masked; V must be finite)
   constexpr int VPR = SP_D * 2 / 16;  // 16-byte vectors per row
-  auto issue_rows = [&](unsigned char* dst, const T* src) {
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    unsigned char* dst = pass == 0 ? Ks : Vs;
+    const T* src = pass == 0 ? pk : pv;
 #pragma unroll 4
     for (int i = lane; i < R * VPR; i += 32) {
       const int r = wbase + i / VPR, v = i % VPR;
@@ -228,8 +233,7 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
         *reinterpret_cast<int4*>(d) = make_int4(0, 0, 0, 0);
     }
     cp_async_commit();
-  };
-  issue_rows(Ks, pk);
+  }
 
   if (early) grid_dependency_wait();
   if (a.pdl) grid_launch_dependents();
@@ -250,7 +254,6 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
       }
     }
   }
-  issue_rows(Vs, pv);
   // the staging slot: the new token's K/V into shared memory and the pool
   if (own0 + wbase <= budget && budget < own0 + wbase + R && budget - own0 < nown) {
     const int r = budget - own0;
@@ -388,7 +391,7 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
     }
   }
 
-  // ---- 4. merge the warps into the CTA's (max, sum, O) and send them -----------------
+  // ---- 4. merge the warps into the CTA's (max, sum, O) ------------------------------
   __syncthreads();  // K / V rows are free: the warp buffers alias them
   float* wo = reinterpret_cast<float*>(smem);  // [W][HS][SP_D]
   float* wm = wo + W * HS * SP_D;              // [W][HS]
@@ -411,38 +414,39 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
     }
   }
   __syncthreads();
-  // ---- 5. one cluster exchange: the CTA's per-head (max, sum) to every CTA, its
-  // O (relative to its own max) slice j to CTA j, all on the receiver's mbarrier
-  cluster_wait_acquire();  // every peer has initialised its mbarrier
-  {
-    const uint32_t b0 = smem_addr(&bar[0]);
-    for (int e4 = tid; e4 < HS * (SP_D / 4); e4 += nthr) {
-      const int head = e4 / (SP_D / 4), d0 = (e4 % (SP_D / 4)) * 4;
-      float M = -INFINITY;
-      for (int w = 0; w < W; ++w) M = fmaxf(M, wm[w * HS + head]);
-      float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f, lsum = 0.f;
-      for (int w = 0; w < W; ++w) {
-        const float m = wm[w * HS + head];
-        const float f = m == -INFINITY ? 0.f : sp_ex2(m - M);
-        lsum = fmaf(wl[w * HS + head], f, lsum);
-        const float4 u = *reinterpret_cast<const float4*>(wo + (w * HS + head) * SP_D + d0);
-        x0 = fmaf(u.x, f, x0); x1 = fmaf(u.y, f, x1); x2 = fmaf(u.z, f, x2); x3 = fmaf(u.w, f, x3);
-      }
-      if (d0 == 0) {
-        const uint32_t src = smem_addr(stin + (c * HS + head) * 2);
-        for (int j = 0; j < CL; ++j)
-          st_async_v2(map_shared(src, j), __float_as_uint(M), __float_as_uint(lsum), map_shared(b0, j));
-      }
-      const int e = head * SP_D + d0, j = e / SL, off = e - j * SL;
-      st_async_v4(map_shared(smem_addr(red + c * SL + off), j), __float_as_uint(x0), __float_as_uint(x1),
-                  __float_as_uint(x2), __float_as_uint(x3), map_shared(b0, j));
+  float* m_cta = cst;
+  float* l_cta = cst + HS;
+  float* gM = cst + 2 * HS;
+  float* gI = cst + 3 * HS;
+  for (int e = tid; e < HS * (SP_D / 4); e += nthr) {
+    const int head = e / (SP_D / 4), d0 = (e % (SP_D / 4)) * 4;
+    float M = -INFINITY;
+    for (int w = 0; w < W; ++w) M = fmaxf(M, wm[w * HS + head]);
+    float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f, lsum = 0.f;
+    for (int w = 0; w < W; ++w) {
+      const float m = wm[w * HS + head];
+      const float f = m == -INFINITY ? 0.f : sp_ex2(m - M);
+      lsum = fmaf(wl[w * HS + head], f, lsum);
+      const float4 u = *reinterpret_cast<const float4*>(wo + (w * HS + head) * SP_D + d0);
+      x0 = fmaf(u.x, f, x0); x1 = fmaf(u.y, f, x1); x2 = fmaf(u.z, f, x2); x3 = fmaf(u.w, f, x3);
+    }
+    *reinterpret_cast<float4*>(ocs + head * SP_D + d0) = make_float4(x0, x1, x2, x3);
+    if (d0 == 0) {
+      m_cta[head] = M;
+      l_cta[head] = lsum;
     }
   }
+  __syncthreads();
+
+  // ---- 5. cluster merge --------------------------------------------------------------
+  cluster_wait_acquire();  // every peer has initialised its mbarriers
+  if (tid < HS) {
+    const uint32_t src = smem_addr(stin + (c * HS + tid) * 2);
+    const uint32_t b0 = smem_addr(&bar[0]);
+    const uint32_t mx = __float_as_uint(m_cta[tid]), ls = __float_as_uint(l_cta[tid]);
+    for (int j = 0; j < CL; ++j) st_async_v2(map_shared(src, j), mx, ls, map_shared(b0, j));
+  }
   mbar_wait_cluster_bounded(&bar[0], 0, a.sess.dev_status);
-  // the group's softmax per head, and the factor that scales CTA j's O to it
-  float* gM = cst;
-  float* gI = cst + HS;
-  float* fj = cst + 2 * HS;  // [CL][HS]
   if (tid < HS) {
     float M = -INFINITY;
     for (int j = 0; j < CL; ++j) M = fmaxf(M, stin[(j * HS + tid) * 2]);
@@ -451,40 +455,10 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
       const float m = stin[(j * HS + tid) * 2];
       lsum = fmaf(stin[(j * HS + tid) * 2 + 1], m == -INFINITY ? 0.f : sp_ex2(m - M), lsum);
     }
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     gM[tid] = M;
-    gI[tid] = inv;
-    for (int j = 0; j < CL; ++j) {
-      const float m = stin[(j * HS + tid) * 2];
-      fj[j * HS + tid] = m == -INFINITY ? 0.f : sp_ex2(m - M) * inv;
-    }
+    gI[tid] = lsum > 0.f ? 1.f / lsum : 0.f;
   }
   __syncthreads();
-  // sum the CL slices of this CTA's part of O in CTA order, each scaled by its
-  // CTA's factor (product rounded, then added: no contraction); heads past G
-  // are padding
-  {
-    const size_t ob = (static_cast<size_t>(s) * Hq + static_cast<size_t>(h) * G) * SP_D;
-    for (int e4 = tid; e4 < red_len / 4; e4 += nthr) {
-      const int e = c * SL + 4 * e4, head = e / SP_D;
-      if (head >= G) continue;
-      float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-      for (int j = 0; j < CL; ++j) {
-        const float f = fj[j * HS + head];
-        const float4 u = *reinterpret_cast<const float4*>(red + j * SL + 4 * e4);
-        x0 = __fadd_rn(x0, __fmul_rn(u.x, f));
-        x1 = __fadd_rn(x1, __fmul_rn(u.y, f));
-        x2 = __fadd_rn(x2, __fmul_rn(u.z, f));
-        x3 = __fadd_rn(x3, __fmul_rn(u.w, f));
-      }
-      const size_t o0 = ob + e;
-      if (a.out_dtype == IC_F32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o0) = make_float4(x0, x1, x2, x3);
-      } else {
-        *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + o0) = make_uint2(sp_pack<T>(x0, x1), sp_pack<T>(x2, x3));
-      }
-    }
-  }
   // received mass of this CTA's slots (exact softmax, heads in order), folded into
   // the running sum over layers after the previous layer's kernel has completed
 #pragma unroll
@@ -506,6 +480,40 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
       if (x != -INFINITY) m += sp_ex2(x - gM[head]) * gI[head];
     }
     macc[r] = a.layer == 0 ? m : __fadd_rn(macc[r], m);
+  }
+  // this CTA's O scaled to the group's softmax, slice j pushed to CTA j
+  {
+    const uint32_t b1 = smem_addr(&bar[1]);
+    for (int e4 = tid; e4 < HS * SP_D / 4; e4 += nthr) {
+      const int e = 4 * e4, head = e / SP_D;
+      const float m = m_cta[head];
+      const float f = m == -INFINITY ? 0.f : sp_ex2(m - gM[head]) * gI[head];
+      const float4 u = *reinterpret_cast<const float4*>(ocs + e);
+      const int j = e / SL, off = e - j * SL;
+      const uint32_t dst = map_shared(smem_addr(red + c * SL + off), j);
+      st_async_v4(dst, __float_as_uint(u.x * f), __float_as_uint(u.y * f), __float_as_uint(u.z * f),
+                  __float_as_uint(u.w * f), map_shared(b1, j));
+    }
+  }
+  mbar_wait_cluster_bounded(&bar[1], 0, a.sess.dev_status);
+  // sum the CL slices of this CTA's part of O in CTA order; heads past G are padding
+  {
+    const size_t ob = (static_cast<size_t>(s) * Hq + static_cast<size_t>(h) * G) * SP_D;
+    for (int e4 = tid; e4 < red_len / 4; e4 += nthr) {
+      const int e = c * SL + 4 * e4, head = e / SP_D;
+      if (head >= G) continue;
+      float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+      for (int j = 0; j < CL; ++j) {
+        const float4 u = *reinterpret_cast<const float4*>(red + j * SL + 4 * e4);
+        x0 += u.x; x1 += u.y; x2 += u.z; x3 += u.w;
+      }
+      const size_t o0 = ob + e;
+      if (a.out_dtype == IC_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o0) = make_float4(x0, x1, x2, x3);
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + o0) = make_uint2(sp_pack<T>(x0, x1), sp_pack<T>(x2, x3));
+      }
+    }
   }
 }
 
