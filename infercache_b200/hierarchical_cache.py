@@ -621,7 +621,7 @@ class GroupedStepper:
         for s in self.streams:
             s.wait_stream(cur)
         if self._replay is None:
-            self._replay = _GraphReplay(self.graphs, self.streams)
+            self._replay = _GraphReplay(self.graphs, self.streams, self.batch.device)
         self._replay(int(replays))
         for s in self.streams:
             cur.wait_stream(s)
@@ -633,8 +633,8 @@ class _GraphReplay:
     then cost no interpreter call each.  Holds the graphs, so their
     executables stay alive."""
 
-    def __init__(self, graphs, streams) -> None:
-        self.graphs, self.streams = list(graphs), list(streams)
+    def __init__(self, graphs, streams, device) -> None:
+        self.graphs, self.streams, self.device = list(graphs), list(streams), torch.device(device)
         n = len(self.graphs)
         self._execs = (ctypes.c_void_p * n)(*[int(g.raw_cuda_graph_exec()) for g in self.graphs])
         self._strms = (ctypes.c_void_p * n)(*[int(st.cuda_stream) for st in self.streams])
@@ -643,8 +643,9 @@ class _GraphReplay:
         if rounds <= 0:
             return
         lib = _lib.load()
-        _lib.raise_for(lib.ic_graph_replay(self._execs, self._strms, len(self.graphs), int(rounds)),
-                       "ic_graph_replay")
+        with torch.cuda.device(self.device):  # the launches run on the graphs' device
+            _lib.raise_for(lib.ic_graph_replay(self._execs, self._strms, len(self.graphs), int(rounds)),
+                           "ic_graph_replay")
 
 
 class GroupedHostStepper:
@@ -744,7 +745,7 @@ class GroupedHostStepper:
         for s in self.streams:
             s.wait_stream(cur)
         if self._replay is None:
-            self._replay = _GraphReplay(self.graphs, self.streams)
+            self._replay = _GraphReplay(self.graphs, self.streams, self.batch.device)
         self._replay(int(steps))
         for s in self.streams:
             cur.wait_stream(s)
