@@ -25,11 +25,11 @@
 //   5. the cluster merges without a cluster-wide barrier on the way: every CTA
 //      pushes its (max, sum) pairs into every peer's shared memory with
 //      st.async, completing on the peer's mbarrier; once all CL pairs have
-//      arrived each CTA knows the group's softmax, adds the received mass of
-//      its own slots (summed over the group's heads in head order) to the
-//      running sum over layers, scales its O and pushes slice j of it to CTA j;
-//      CTA j sums the CL slices it receives in CTA order (deterministic) and
-//      writes its part of `out`.
+//      arrived each CTA knows the group's softmax, scales its O and pushes
+//      slice j of it to CTA j, then, while the slices travel, adds the received
+//      mass of its own slots (summed over the group's heads in head order) to
+//      the running sum over layers; CTA j sums the CL slices it receives in CTA
+//      order (deterministic) and writes its part of `out`.
 // No global scratch and no atomics.
 #include <math.h>
 
@@ -459,6 +459,20 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
     gI[tid] = lsum > 0.f ? 1.f / lsum : 0.f;
   }
   __syncthreads();
+  // this CTA's O scaled to the group's softmax, slice j pushed to CTA j
+  {
+    const uint32_t b1 = smem_addr(&bar[1]);
+    for (int e4 = tid; e4 < HS * SP_D / 4; e4 += nthr) {
+      const int e = 4 * e4, head = e / SP_D;
+      const float m = m_cta[head];
+      const float f = m == -INFINITY ? 0.f : sp_ex2(m - gM[head]) * gI[head];
+      const float4 u = *reinterpret_cast<const float4*>(ocs + e);
+      const int j = e / SL, off = e - j * SL;
+      const uint32_t dst = map_shared(smem_addr(red + c * SL + off), j);
+      st_async_v4(dst, __float_as_uint(u.x * f), __float_as_uint(u.y * f), __float_as_uint(u.z * f),
+                  __float_as_uint(u.w * f), map_shared(b1, j));
+    }
+  }
   // received mass of this CTA's slots (exact softmax, heads in order), folded into
   // the running sum over layers after the previous layer's kernel has completed
 #pragma unroll
@@ -480,20 +494,6 @@ __global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_
       if (x != -INFINITY) m += sp_ex2(x - gM[head]) * gI[head];
     }
     macc[r] = a.layer == 0 ? m : __fadd_rn(macc[r], m);
-  }
-  // this CTA's O scaled to the group's softmax, slice j pushed to CTA j
-  {
-    const uint32_t b1 = smem_addr(&bar[1]);
-    for (int e4 = tid; e4 < HS * SP_D / 4; e4 += nthr) {
-      const int e = 4 * e4, head = e / SP_D;
-      const float m = m_cta[head];
-      const float f = m == -INFINITY ? 0.f : sp_ex2(m - gM[head]) * gI[head];
-      const float4 u = *reinterpret_cast<const float4*>(ocs + e);
-      const int j = e / SL, off = e - j * SL;
-      const uint32_t dst = map_shared(smem_addr(red + c * SL + off), j);
-      st_async_v4(dst, __float_as_uint(u.x * f), __float_as_uint(u.y * f), __float_as_uint(u.z * f),
-                  __float_as_uint(u.w * f), map_shared(b1, j));
-    }
   }
   mbar_wait_cluster_bounded(&bar[1], 0, a.sess.dev_status);
   // sum the CL slices of this CTA's part of O in CTA order; heads past G are padding
