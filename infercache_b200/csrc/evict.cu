@@ -159,11 +159,40 @@ __global__ void __launch_bounds__(EV_THREADS) evict_kernel(const ic_evict_args a
   // decay + boost of every occupied slot (already applied when REDUCED); each
   // thread updates the slots it staged
   if (!REDUCED) {
-    for (int j = tid; j < B; j += EV_THREADS) {
-      if (!occ_s[j]) continue;
-      const float v = updated_importance(a, s, j, imp_s[j]);
-      imp[j] = v;
-      imp_s[j] = v;
+    constexpr int EV_MH = 8, EV_PER = 3;  // heads and slots per thread on the fast path
+    if (a.mass && a.mass_layers == 1 && a.mass_heads <= EV_MH && B <= EV_PER * EV_THREADS) {
+      // one mass column per head: every load of the thread's slots is issued
+      // before any is used, then the same sums in head order as below
+      const int MH = a.mass_heads;
+      const float* base = a.mass + static_cast<size_t>(s) * MH * ntot;
+      float mv[EV_PER][EV_MH];
+#pragma unroll
+      for (int i = 0; i < EV_PER; ++i) {
+        const int j = tid + i * EV_THREADS;
+        const bool on = j < B && occ_s[j];
+#pragma unroll
+        for (int hh = 0; hh < EV_MH; ++hh)
+          mv[i][hh] = on && hh < MH ? base[static_cast<size_t>(hh) * ntot + j] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < EV_PER; ++i) {
+        const int j = tid + i * EV_THREADS;
+        if (j >= B || !occ_s[j]) continue;
+        float tot = mv[i][0];
+#pragma unroll
+        for (int hh = 1; hh < EV_MH; ++hh)
+          if (hh < MH) tot = __fadd_rn(tot, mv[i][hh]);
+        const float v = __fadd_rn(__fmul_rn(imp_s[j], a.decay), __fdiv_rn(tot, a.mass_div));
+        imp[j] = v;
+        imp_s[j] = v;
+      }
+    } else {
+      for (int j = tid; j < B; j += EV_THREADS) {
+        if (!occ_s[j]) continue;
+        const float v = updated_importance(a, s, j, imp_s[j]);
+        imp[j] = v;
+        imp_s[j] = v;
+      }
     }
   }
   if (tid == 0 && a.advance_pos) a.new_pos[s] = snap_newpos + 1;  // the next step's position
