@@ -526,6 +526,59 @@ def test_evict_kernel_ties_exact():
     assert np.array_equal(got[mask], want.astype(np.float32)[mask])
 
 
+@pytest.mark.parametrize("ml,mh", [(1, 4), (1, 8), (5, 3), (8, 2)])
+def test_evict_mass_layouts(ml, mh):
+    """Kernel B's importance update for each mass layout it handles: one column
+    per KV head (the decode step's; loads batched per thread), columns of a few
+    layers, and many layers (a separate wide update kernel first), over a budget
+    of more than two slots per thread: importance * decay + (sum over layers in
+    order, then heads in order) / div, each step rounded, on every occupied slot
+    but the ones the step rewrites."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    from infercache_b200 import _lib
+    cfg = CacheConfig(num_layers=2, num_kv_heads=2, head_dim=128, sink_size=4, recent_size=64,
+                      important_size=1100, decay=0.9, dtype=torch.float16)
+    S = 3
+    b = SessionBatch(cfg, S, "cuda:0")
+    B = cfg.total_budget
+    g = torch.Generator().manual_seed(40 + ml)
+    imp = torch.rand(S, B, generator=g) + 0.5
+    occ = torch.rand(S, B, generator=g) < 0.9
+    b.importance.copy_(imp)
+    b.occupied.copy_(occ)
+    b.positions.copy_(torch.arange(B).repeat(S, 1) + 10)
+    b.ctrl[:, _lib.IC_CTRL_RECENT_FILL] = cfg.recent_size
+    b.ctrl[:, _lib.IC_CTRL_IMPORTANT_FILL] = cfg.important_size
+    b.ctrl[:, _lib.IC_CTRL_RECENT_PTR] = 7
+    m = torch.rand(S, mh, B + 1, ml, generator=g)
+    mcol = m.to("cuda").contiguous()
+    npos = torch.arange(S, device="cuda", dtype=torch.int64) + 5000
+    div = float(ml * mh)
+    e = _lib.ic_evict_args(tiers=b._c_tiers, sess=b._c_sess, mass=mcol.data_ptr(), mass_heads=mh, mass_layers=ml,
+                           mass_div=div, decay=0.9, pdl=0, new_pos=npos.data_ptr(), events=b.events.data_ptr())
+    _lib.call("ic_evict_update", e)
+    torch.cuda.synchronize()
+    b.check_device_status()
+    mn = m.numpy()
+    tot = None
+    for hh in range(mh):
+        acc = mn[:, hh, :B, 0].astype(np.float32)
+        for l in range(1, ml):
+            acc = (acc + mn[:, hh, :B, l]).astype(np.float32)
+        tot = acc if tot is None else (tot + acc).astype(np.float32)
+    want = ((imp.numpy() * np.float32(0.9)).astype(np.float32) + (tot / np.float32(div)).astype(np.float32))
+    want = np.where(occ.numpy(), want.astype(np.float32), imp.numpy())
+    got = b.importance.cpu().numpy()
+    ev = b.events.cpu().numpy()
+    mask = np.ones_like(got, bool)
+    for s_ in range(S):
+        mask[s_, 7] = False  # the ring slot the step rewrites
+        if ev[s_, 0] in (2, 3):
+            mask[s_, ev[s_, 2]] = False
+            assert got[s_, ev[s_, 2]] == want[s_, 7]
+    assert np.array_equal(got[mask], want[mask])
+
+
 def test_paged_trace_gpu(golden):
     """MultiSessionCache / KVAllocator / PagePool against the reference trace."""
     import json
