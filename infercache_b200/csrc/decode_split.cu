@@ -5,8 +5,8 @@
 // The launch fills the machine on its own: the budget + 1 logical slots of a
 // (session, KV head) group are cut into CL chunks of 16-slot blocks, one CTA
 // per chunk, the group's CTAs one thread-block cluster.  At 16 sessions x 2 KV
-// heads x 1041 slots with CL = 8: 256 CTAs of nine warps, 144 slots each (one
-// 16-slot block per warp; two per warp only when a chunk has more than nine).
+// heads x 1041 slots CL = 4: 128 CTAs of nine warps, 272 slots each (two
+// 16-slot blocks per warp), one CTA per SM; with fewer than 16 groups CL = 8.
 // Per CTA:
 //   1. every warp looks up its one or two 16-slot blocks in the session's slot
 //      table and copies their K rows, then their V rows, into padded shared-
@@ -56,15 +56,26 @@ struct SplitGeom {
   int cl, chunk, blocks, rb, w, slice;
 };
 
-__host__ __device__ inline SplitGeom split_geometry(int ntot, int hs, int cl_req) {
+__host__ __device__ inline SplitGeom split_geometry(int ntot, int hs, int cl_req, int groups) {
   SplitGeom g;
-  // default: 8 CTAs per group (portable cluster size) while they hold at most
-  // 16 blocks of 16 slots each, else as many as 16-block CTAs need
-  const int cl0 = cl_req > 0 ? cl_req : (ntot <= 8 * 256 ? 8 : (ntot + 255) / 256);
+  // default, from timings of chained one-layer launches (16 query / 2 KV
+  // heads, budget 1040, 4 to 32 sessions): with 16 groups or more, 4 CTAs
+  // per group while 4 CTAs of at most 18 blocks hold the slots (one CTA of 9
+  // warps per SM); else 8 CTAs per group (portable cluster size) while they
+  // hold at most 16 blocks each, else as many as 16-block CTAs need
+  int cl0;
+  if (cl_req > 0)
+    cl0 = cl_req;
+  else if (groups >= 16 && ntot <= 4 * 16 * 2 * SP_MAXW)
+    cl0 = 4;
+  else
+    cl0 = ntot <= 8 * 256 ? 8 : (ntot + 255) / 256;
   g.blocks = (ntot + 16 * cl0 - 1) / (16 * cl0);
   g.chunk = 16 * g.blocks;
   g.cl = (ntot + g.chunk - 1) / g.chunk;
-  g.rb = g.blocks > SP_MAXW ? 2 : 1;
+  // two 16-slot blocks per warp once a CTA holds more than four: fewer warps
+  // to merge measured faster at every cluster size tried
+  g.rb = g.blocks > 4 ? 2 : 1;
   g.w = (g.blocks + g.rb - 1) / g.rb;
   g.slice = sp_align((hs * SP_D + g.cl - 1) / g.cl, 4);  // O floats reduced by each CTA
   return g;
@@ -567,7 +578,7 @@ int launch_decode_split(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_INVALID_ARG;
   }
   const int hs = G <= 8 ? 8 : 16;
-  const SplitGeom g = split_geometry(a.tiers.budget + 1, hs, a.cluster_size);
+  const SplitGeom g = split_geometry(a.tiers.budget + 1, hs, a.cluster_size, a.sess.num_sessions * a.pool.num_kv_heads);
   if (g.blocks > 2 * SP_MAXW || g.cl > SP_MAXCL) {
     set_last_error("decode (split): budget too large for 16 CTAs of 256 slots");
     return IC_ERR_UNSUPPORTED;
