@@ -777,6 +777,58 @@ def test_attend_layer_at_a_time_vs_oracle(variant, knob):
     b3.check_device_status()
 
 
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_attend_split_default_geometry_two_head_blocks(dtype):
+    """The slot-split kernel's default geometry at 32 (session, KV head) groups
+    (4 CTAs per group, two 16-slot blocks per warp, one CTA per SM) with 16
+    query heads per KV head (two n = 8 blocks, the largest shared-memory
+    layout), fp16 and bf16: outputs (fp32) within 1e-3 of the one-cluster-per-
+    group kernel, identical events, slot tables and positions, importance
+    within 1e-3, and a second run bit for bit."""
+    from infercache_b200 import CacheConfig, SessionBatch
+    from infercache_b200 import _lib
+    L, Hq, Hkv, D, S, T, steps = 4, 32, 2, 128, 16, 1200, 3
+    dt = torch.float16 if dtype == "float16" else torch.bfloat16
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=4, recent_size=256,
+                      important_size=780, decay=0.99, dtype=dt)
+    g = torch.Generator().manual_seed(21)
+    prompts = [(torch.randn(L, Hkv, T, D, generator=g).to(dt), torch.randn(L, Hkv, T, D, generator=g).to(dt),
+                torch.rand(T, generator=g)) for _ in range(S)]
+    q = torch.randn(steps, L, S, Hq, D, generator=g).to(dt).cuda()
+    k = torch.randn(steps, L, S, Hkv, D, generator=g).to(dt).cuda()
+    v = torch.randn(steps, L, S, Hkv, D, generator=g).to(dt).cuda()
+
+    def run(variant):
+        b = SessionBatch(cfg, S, "cuda:0")
+        b.kernel_variant = variant
+        for s_ in range(S):
+            b.load_prompt(s_, tuple((prompts[s_][0][l][None].cuda(), prompts[s_][1][l][None].cuda())
+                                    for l in range(L)), prompts[s_][2])
+        outs, evs = [], []
+        for t in range(steps):
+            o = torch.empty(L, S, Hq, D, dtype=torch.float32, device="cuda:0")
+            for l in range(L):
+                b.attend(l, q[t, l], k[t, l], v[t, l], out=o[l])
+            b.evict([T + t] * S)
+            outs.append(o)
+            evs.append(b.events.clone())
+        torch.cuda.synchronize()
+        b.check_device_status()
+        return b, outs, evs
+
+    b1, outs1, evs1 = run(_lib.IC_DECODE_AUTO)
+    b2, outs2, evs2 = run(_lib.IC_DECODE_TENSOR_CORES)
+    for t in range(steps):
+        assert rows_close(outs1[t].cpu().numpy(), outs2[t].cpu().numpy(), 1e-3), t
+        assert torch.equal(evs1[t], evs2[t]), t
+    assert torch.equal(b1.slot_table, b2.slot_table) and torch.equal(b1.positions, b2.positions)
+    assert elem_close(b1.importance.cpu().numpy(), b2.importance.cpu().numpy(), 1e-3)
+    b3, outs3, _ = run(_lib.IC_DECODE_AUTO)
+    for t in range(steps):
+        assert torch.equal(outs1[t], outs3[t]), t
+    assert torch.equal(b1.importance, b3.importance)
+
+
 def run_small_attend(sp, dtype, variant=0):
     """run_small with each step taken layer by layer through attend()."""
     from gpu_protocol import TORCH_DT
