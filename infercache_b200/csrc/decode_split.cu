@@ -5,8 +5,8 @@
 // The launch fills the machine on its own: the budget + 1 logical slots of a
 // (session, KV head) group are cut into CL chunks of 16-slot blocks, one CTA
 // per chunk, the group's CTAs one thread-block cluster.  At 16 sessions x 2 KV
-// heads x 1041 slots CL = 4: 128 CTAs of nine warps, 272 slots each (two
-// 16-slot blocks per warp), one CTA per SM; with fewer than 16 groups CL = 8.
+// heads x 1041 slots CL = 3: 96 CTAs of eleven warps, 352 slots each (two
+// 16-slot blocks per warp), one CTA per SM; CL = 4 from 16 groups, else 8.
 // Per CTA:
 //   1. every warp looks up its one or two 16-slot blocks in the session's slot
 //      table and copies their K rows, then their V rows, into padded shared-
@@ -43,7 +43,7 @@ namespace ic {
 namespace {
 
 constexpr int SP_D = 128;
-constexpr int SP_MAXW = 9;                  // warps per CTA at most
+constexpr int SP_MAXW = 12;                 // warps per CTA at most
 constexpr int SP_MAXCL = 16;                // CTAs per cluster at most
 constexpr int SP_PITCH = SP_D * 2 + 16;     // padded row: conflict-free ldmatrix
 constexpr float SP_LOG2E = 1.4426950408889634f;
@@ -56,20 +56,11 @@ struct SplitGeom {
   int cl, chunk, blocks, rb, w, slice;
 };
 
-__host__ __device__ inline SplitGeom split_geometry(int ntot, int hs, int cl_req, int groups) {
+__host__ __device__ inline SplitGeom split_geometry(int ntot, int hs, int cl_req) {
   SplitGeom g;
-  // default, from timings of chained one-layer launches (16 query / 2 KV
-  // heads, budget 1040, 4 to 32 sessions): with 16 groups or more, 4 CTAs
-  // per group while 4 CTAs of at most 18 blocks hold the slots (one CTA of 9
-  // warps per SM); else 8 CTAs per group (portable cluster size) while they
-  // hold at most 16 blocks each, else as many as 16-block CTAs need
-  int cl0;
-  if (cl_req > 0)
-    cl0 = cl_req;
-  else if (groups >= 16 && ntot <= 4 * 16 * 2 * SP_MAXW)
-    cl0 = 4;
-  else
-    cl0 = ntot <= 8 * 256 ? 8 : (ntot + 255) / 256;
+  // cl_req CTAs per group; 0: 8 (portable cluster size) while they hold at most
+  // 16 blocks of 16 slots each, else as many as 16-block CTAs need
+  const int cl0 = cl_req > 0 ? cl_req : (ntot <= 8 * 256 ? 8 : (ntot + 255) / 256);
   g.blocks = (ntot + 16 * cl0 - 1) / (16 * cl0);
   g.chunk = 16 * g.blocks;
   g.cl = (ntot + g.chunk - 1) / g.chunk;
@@ -148,7 +139,7 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_
 }
 
 template <typename T, int NG, int RB>
-__global__ void __launch_bounds__(SP_MAXW * 32, 2) decode_split_kernel(const ic_decode_args a, SplitGeom geo) {
+__global__ void __launch_bounds__(SP_MAXW * 32, 1) decode_split_kernel(const ic_decode_args a, SplitGeom geo) {
   constexpr int HS = NG * 8;        // query heads per group, padded to the mma's n = 8
   constexpr int R = 16 * RB;        // slots per warp
   constexpr bool SPLITP = std::is_same<T, __nv_bfloat16>::value;  // P as high + low bf16
@@ -578,9 +569,29 @@ int launch_decode_split(const ic_decode_args& a, cudaStream_t stream) {
     return IC_ERR_INVALID_ARG;
   }
   const int hs = G <= 8 ? 8 : 16;
-  const SplitGeom g = split_geometry(a.tiers.budget + 1, hs, a.cluster_size, a.sess.num_sessions * a.pool.num_kv_heads);
+  const int ntot = a.tiers.budget + 1, groups = a.sess.num_sessions * a.pool.num_kv_heads;
+  auto fits = [&](const SplitGeom& x) {
+    return x.blocks <= 2 * SP_MAXW && x.cl <= SP_MAXCL && split_smem(x, hs).total <= 227 * 1024;
+  };
+  // Default CTAs per group, from timings of chained one-layer launches (16
+  // query / 2 KV heads, budget 1040, 4 to 32 sessions): fewer, larger CTAs
+  // win once there are enough groups to fill the GPU -- 3 per group from 32
+  // groups, 4 from 16 -- each taken only if its CTAs fit; else the rule of
+  // split_geometry.
+  SplitGeom g = split_geometry(ntot, hs, a.cluster_size);
+  if (a.cluster_size == 0) {
+    const int prefer[2] = {groups >= 32 ? 3 : 0, groups >= 16 ? 4 : 0};
+    for (int c : prefer) {
+      if (c == 0) continue;
+      const SplitGeom x = split_geometry(ntot, hs, c);
+      if (fits(x)) {
+        g = x;
+        break;
+      }
+    }
+  }
   if (g.blocks > 2 * SP_MAXW || g.cl > SP_MAXCL) {
-    set_last_error("decode (split): budget too large for 16 CTAs of 256 slots");
+    set_last_error("decode (split): budget too large for 16 CTAs of 384 slots");
     return IC_ERR_UNSUPPORTED;
   }
   const SplitSmem L = split_smem(g, hs);
