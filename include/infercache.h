@@ -167,8 +167,8 @@ enum ic_decode_variant {
   IC_DECODE_TENSOR_SPLIT = 5     /* fp16 / bf16, a cluster of CTAs over chunks of
                                     the group's slots, merged through distributed
                                     shared memory; cluster_size = CTAs per group
-                                    (0 = choose: 3 from 32 groups, 4 from 16,
-                                    where their CTAs fit, else 8; at most 16)   */
+                                    (0 = choose: the fewest per group, up to 8,
+                                    that fit and give 64 CTAs; at most 16)      */
 };
 int ic_decode_layer(const ic_decode_args* a, void* stream);
 

@@ -6,7 +6,8 @@
 // (session, KV head) group are cut into CL chunks of 16-slot blocks, one CTA
 // per chunk, the group's CTAs one thread-block cluster.  At 16 sessions x 2 KV
 // heads x 1041 slots CL = 3: 96 CTAs of eleven warps, 352 slots each (two
-// 16-slot blocks per warp), one CTA per SM; CL = 4 from 16 groups, else 8.
+// 16-slot blocks per warp), one CTA per SM (by default the fewest CTAs per
+// group that fit, with at least 64 CTAs in the launch).
 // Per CTA:
 //   1. every warp looks up its one or two 16-slot blocks in the session's slot
 //      table and copies their K rows, then their V rows, into padded shared-
@@ -574,17 +575,16 @@ int launch_decode_split(const ic_decode_args& a, cudaStream_t stream) {
     return x.blocks <= 2 * SP_MAXW && x.cl <= SP_MAXCL && split_smem(x, hs).total <= 227 * 1024;
   };
   // Default CTAs per group, from timings of chained one-layer launches (16
-  // query / 2 KV heads, budget 1040, 4 to 32 sessions): fewer, larger CTAs
-  // win once there are enough groups to fill the GPU -- 3 per group from 32
-  // groups, 4 from 16 -- each taken only if its CTAs fit; else the rule of
+  // query / 2 KV heads, budgets 1040 and 2048, 4 to 32 sessions): fewer,
+  // larger CTAs win as long as the launch still has 64 CTAs or more -- the
+  // fewest per group (up to 8) that fit and reach 64; else the rule of
   // split_geometry.
   SplitGeom g = split_geometry(ntot, hs, a.cluster_size);
   if (a.cluster_size == 0) {
-    const int prefer[2] = {groups >= 32 ? 3 : 0, groups >= 16 ? 4 : 0};
-    for (int c : prefer) {
-      if (c == 0) continue;
+    for (int c = 1; c <= 8; ++c) {
+      if (groups * c < 64) continue;
       const SplitGeom x = split_geometry(ntot, hs, c);
-      if (fits(x)) {
+      if (x.cl == c && fits(x)) {
         g = x;
         break;
       }

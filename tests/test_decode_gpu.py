@@ -777,20 +777,24 @@ def test_attend_layer_at_a_time_vs_oracle(variant, knob):
     b3.check_device_status()
 
 
-@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
-def test_attend_split_default_geometry_two_head_blocks(dtype):
-    """The slot-split kernel's default geometry at 32 (session, KV head) groups
-    (4 CTAs per group, two 16-slot blocks per warp, one CTA per SM) with 16
-    query heads per KV head (two n = 8 blocks, the largest shared-memory
-    layout), fp16 and bf16: outputs (fp32) within 1e-3 of the one-cluster-per-
-    group kernel, identical events, slot tables and positions, importance
-    within 1e-3, and a second run bit for bit."""
+@pytest.mark.parametrize("dtype,hq,S,recent,important,T", [
+    ("float16", 32, 16, 256, 780, 1200), ("bfloat16", 32, 16, 256, 780, 1200),
+    ("float16", 16, 8, 512, 1532, 2200), ("bfloat16", 32, 8, 512, 1532, 2200)])
+def test_attend_split_default_geometry_two_head_blocks(dtype, hq, S, recent, important, T):
+    """The slot-split kernel's default geometry (the fewest CTAs per group that
+    fit with 64 CTAs or more; two 16-slot blocks per warp, one CTA per SM): at
+    budget 1040 with 32 groups and 16 query heads per KV head (two n = 8
+    blocks), and at budget 2048 with 16 groups (6 CTAs per group of eleven
+    warps; 7 with two head blocks, whose shared memory rules 6 out), fp16 and
+    bf16: outputs (fp32) within 1e-3 of the one-cluster-per-group kernel,
+    identical events, slot tables and positions, importance within 1e-3, and a
+    second run bit for bit."""
     from infercache_b200 import CacheConfig, SessionBatch
     from infercache_b200 import _lib
-    L, Hq, Hkv, D, S, T, steps = 4, 32, 2, 128, 16, 1200, 3
+    L, Hq, Hkv, D, steps = 4, hq, 2, 128, 3
     dt = torch.float16 if dtype == "float16" else torch.bfloat16
-    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=4, recent_size=256,
-                      important_size=780, decay=0.99, dtype=dt)
+    cfg = CacheConfig(num_layers=L, num_kv_heads=Hkv, head_dim=D, sink_size=4, recent_size=recent,
+                      important_size=important, decay=0.99, dtype=dt)
     g = torch.Generator().manual_seed(21)
     prompts = [(torch.randn(L, Hkv, T, D, generator=g).to(dt), torch.randn(L, Hkv, T, D, generator=g).to(dt),
                 torch.rand(T, generator=g)) for _ in range(S)]
