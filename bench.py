@@ -1220,9 +1220,10 @@ def main():
                                        f"({groups} launches of {S // groups} sessions when grouped)",
                              "alg_bytes_per_launch": alg_bytes, "launch_us": dec_launch_s * 1e6,
                              "launch_us_basis": "step time / 36 inside the step graphs, eviction included",
-                             "sequential_attend_kernel": "decode_split_kernel: a cluster of 8 CTAs per (session, "
-                                                         "KV head) over slot chunks, merged through distributed "
-                                                         "shared memory (attend, one layer at a time)",
+                             "sequential_attend_kernel": "decode_split_kernel: a cluster of CTAs per (session, "
+                                                         "KV head) over slot chunks (3 at this shape, one per SM), "
+                                                         "merged through distributed shared memory (attend, one "
+                                                         "layer at a time)",
                              "sequential_attend_us": seq_launch_s * 1e6,
                              "sequential_attend_frac": alg_bytes / seq_launch_s / 1e9 / peak,
                              "traffic_basis": "dram__bytes_read + dram__bytes_write of one decode_lean_kernel launch "
